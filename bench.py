@@ -1,0 +1,501 @@
+"""Benchmark of the gtx16_fp16 hot path on B200 (prints one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (a "step" is one call of the hot path on one batch of synthetic input):
+  gemm4096   gtx16_fp16.matmul, fp16 4096x4096x4096 -> fp16 (config 3; the headline metric)   [default]
+  skinny     mm_t M=8, K=N=4096, fp32 x, fp16 w_t, fp32 bias/out (config 2)
+  splitk     mm_t 128x16384x1024 fp16 -> fp16 (config 3, split-K shape)
+  rescale    mm_t 2048x3072x1024 fp32 x with 1% rows x [100,200] (config 4)
+Multi-GPU (--gpus N under torchrun): every listed workload runs as N independent replicas (the path
+has no exchange step for these shapes; scaling "weak"), value = sum over ranks (max-over-ranks time).
+
+Timing: W untimed warm-up steps, then K steps between barrier + synchronize, timed with CUDA events
+on the launching stream. Inputs rotate over several sets whose total exceeds the 126 MB L2, so every
+step reads its operands from HBM. Clocks and throttle reasons are sampled with NVML during the timed
+region. `e2e` repeats the step through the public API from pinned host memory (H2D of the inputs and
+D2H of the result inside the timed region). `cpu_baseline` times the reference's CPU path
+(oracle/cpu_path.py: torch fp32 matmul) on a bounded sample on the host cores (rank 0, N=1 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "gtx16-fp16_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def load_profile_traffic():
+    """Per-launch DRAM bytes of each workload's dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except ValueError:
+            return {}
+    return {}
+
+
+# ---------------------------------------------------------------------------------------------
+# Clock sampling (NVML) during the timed region
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, device_index: int, interval_s: float = 0.005):
+        self.interval = interval_s
+        self.samples: list[tuple[int, int]] = []
+        self.sm_max = None
+        self.ok = False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            uuid = None
+            try:
+                uuid = torch.cuda.get_device_properties(device_index).uuid
+            except Exception:
+                pass
+            self.h = None
+            if uuid is not None:
+                try:
+                    self.h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + str(uuid)).encode())
+                except Exception:
+                    self.h = None
+            if self.h is None:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[device_index]) if vis and vis.split(",")[0].isdigit() else device_index
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.sm_max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.ok = True
+        except Exception as e:  # no NVML: report that instead of clocks
+            self.err = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                sm = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = int(self._reasons_fn(self.h))
+                self.samples.append((sm, rs))
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"error": getattr(self, "err", "nvml unavailable")}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.sm_max, "reasons": [], "samples": 0}
+        sms = sorted(s for s, _ in self.samples)
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = [name for bit, name in self.REASONS.items() if mask & bit and name != "gpu_idle"]
+        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": self.sm_max, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------------
+# Workloads
+# ---------------------------------------------------------------------------------------------
+class Workload:
+    name = ""
+    metric = ""
+    unit = ""
+    bound = "tensor"
+
+    def __init__(self, dev):
+        self.dev = dev
+
+    def flops(self) -> float:
+        return 0.0
+
+    def alg_bytes(self) -> float:
+        return 0.0
+
+
+def _rotating_sets(nbytes_per_set: int) -> int:
+    return max(3, int(2 * L2_BYTES // max(nbytes_per_set, 1)) + 1)
+
+
+class Gemm(Workload):
+    """gtx16_fp16.matmul: fp16 A[M,K] @ fp16 B[K,N] -> fp16."""
+    bound = "tensor"
+
+    def __init__(self, dev, M, K, N, name):
+        super().__init__(dev)
+        self.M, self.K, self.N = M, K, N
+        self.name = name
+        self.metric = f"GEMM TFLOPS (fp16 {M}x{K}x{N}, gtx16_fp16.matmul)"
+        self.unit = "TFLOPS"
+        per = (M * K + K * N + M * N) * 2
+        self.nsets = _rotating_sets(per)
+        g = torch.Generator(device=dev).manual_seed(0)
+        self.A = [torch.randn(M, K, device=dev, generator=g).half() for _ in range(self.nsets)]
+        self.B = [(torch.randn(K, N, device=dev, generator=g) * K ** -0.5).half() for _ in range(self.nsets)]
+        self.i = 0
+
+    def config(self):
+        return {"workload": self.name, "M": self.M, "K": self.K, "N": self.N, "in": "fp16", "out": "fp16",
+                "inputs": "A~N(0,1), B~N(0,1/sqrt(K)) fp16, seed 0 (BASELINE config 3)",
+                "l2": f"{self.nsets} rotating input sets ({self.nsets * (self.M * self.K + self.K * self.N) * 2 >> 20} MiB) > 126 MB L2"}
+
+    def flops(self):
+        return 2.0 * self.M * self.N * self.K
+
+    def alg_bytes(self):
+        return 2.0 * (self.M * self.K + self.K * self.N + self.M * self.N)
+
+    def step(self, g16):
+        j = self.i % self.nsets
+        self.i += 1
+        return g16.matmul(self.A[j], self.B[j])
+
+    # e2e through the public API from pinned host memory
+    def host_inputs(self):
+        return [self.A[0].cpu().pin_memory(), self.B[0].cpu().pin_memory()]
+
+    def host_out(self):
+        return torch.empty(self.M, self.N, dtype=torch.float16).pin_memory()
+
+    def e2e_step(self, g16, hin, hout):
+        a = hin[0].to(self.dev, non_blocking=True)
+        b = hin[1].to(self.dev, non_blocking=True)
+        hout.copy_(g16.matmul(a, b), non_blocking=True)
+
+    def cpu_sample(self):
+        """The reference CPU path on a bounded sample: fp32 torch.matmul of 512 rows x full B."""
+        rows = min(self.M, 512)
+        a = self.A[0][:rows].float().cpu()
+        b = self.B[0].float().cpu()
+        return (lambda: torch.matmul(a, b)), 2.0 * rows * self.N * self.K, f"fp32 torch.matmul {rows}x{self.K}x{self.N} (rows of the workload)"
+
+
+class MmT(Workload):
+    """gtx16_fp16.mm_t(x, w_t, bias, out_dtype) (BASELINE configs 2 and 4)."""
+
+    def __init__(self, dev, M, K, N, name, xdt, out_dtype, wstd, bias_std, rescale=False):
+        super().__init__(dev)
+        self.M, self.K, self.N = M, K, N
+        self.name = name
+        self.xdt, self.out_dtype = xdt, out_dtype
+        self.skinny = M <= 8
+        self.bound = "hbm" if self.skinny else "tensor"
+        self.metric = (f"skinny mm_t HBM GB/s (M={M}, {K}x{N})" if self.skinny else
+                       f"mm_t TFLOPS ({M}x{K}x{N}{', overflow rescale' if rescale else ''})")
+        self.unit = "GB/s" if self.skinny else "TFLOPS"
+        xs = 4 if xdt == torch.float32 else 2
+        per = M * K * xs + K * N * 2 + M * N * 4
+        self.nsets = _rotating_sets(per)
+        g = torch.Generator(device=dev).manual_seed(0)
+        self.X, self.W = [], []
+        for _ in range(self.nsets):
+            x = torch.randn(M, K, device=dev, generator=g)
+            if rescale:
+                rows = torch.randperm(M, device=dev, generator=g)[: max(1, M // 100)]
+                f = torch.exp(torch.empty(len(rows), device=dev).uniform_(4.6051702, 5.2983174, generator=g))
+                x[rows] *= f[:, None]
+            self.X.append(x.to(xdt))
+            self.W.append((torch.randn(K, N, device=dev, generator=g) * wstd).half())
+        self.b = torch.randn(N, device=dev, generator=g) * bias_std if bias_std else torch.zeros(N, device=dev)
+        self.rescale = rescale
+        self.i = 0
+
+    def config(self):
+        return {"workload": self.name, "M": self.M, "K": self.K, "N": self.N,
+                "in": "fp32" if self.xdt == torch.float32 else "fp16", "w": "fp16",
+                "out": "fp32" if self.out_dtype == torch.float32 else "fp16",
+                "l2": f"{self.nsets} rotating input sets > 126 MB L2"}
+
+    def flops(self):
+        return 2.0 * self.M * self.N * self.K
+
+    def alg_bytes(self):
+        xs = 4 if self.xdt == torch.float32 else 2
+        os_ = 4 if self.out_dtype == torch.float32 else 2
+        return float(2 * self.K * self.N + xs * self.M * self.K + 4 * self.N + os_ * self.M * self.N)
+
+    def step(self, g16):
+        j = self.i % self.nsets
+        self.i += 1
+        return g16.mm_t(self.X[j], self.W[j], self.b, self.out_dtype)
+
+    def host_inputs(self):
+        return [self.X[0].cpu().pin_memory(), self.W[0].cpu().pin_memory()]
+
+    def host_out(self):
+        return torch.empty(self.M, self.N, dtype=self.out_dtype).pin_memory()
+
+    def e2e_step(self, g16, hin, hout):
+        x = hin[0].to(self.dev, non_blocking=True)
+        w = hin[1].to(self.dev, non_blocking=True)
+        hout.copy_(g16.mm_t(x, w, self.b, self.out_dtype), non_blocking=True)
+
+    def cpu_sample(self):
+        rows = min(self.M, 512)
+        x = self.X[0][:rows].float().cpu()
+        w = self.W[0].float().cpu()
+        b = self.b.cpu()
+        from oracle import cpu_path
+        return (lambda: cpu_path.mm_t_fp32(x, w.half(), b)), 2.0 * rows * self.N * self.K, \
+            f"fp32 F.linear {rows}x{self.K}x{self.N} (reference linear.py fallback)"
+
+
+WORKLOADS = {
+    "gemm4096": lambda dev: Gemm(dev, 4096, 4096, 4096, "gemm4096"),
+    "splitk": lambda dev: Gemm(dev, 128, 16384, 1024, "splitk"),
+    "splitk64": lambda dev: Gemm(dev, 64, 1024, 1024, "splitk64"),
+    "gemm16384": lambda dev: Gemm(dev, 16384, 16384, 16384, "gemm16384"),
+    "skinny": lambda dev: MmT(dev, 8, 4096, 4096, "skinny", torch.float32, torch.float32, 0.02, 0.01),
+    "skinny1": lambda dev: MmT(dev, 1, 4096, 4096, "skinny1", torch.float32, torch.float32, 0.02, 0.01),
+    "skinny4": lambda dev: MmT(dev, 4, 4096, 4096, "skinny4", torch.float32, torch.float32, 0.02, 0.01),
+    "rescale": lambda dev: MmT(dev, 2048, 3072, 1024, "rescale", torch.float32, torch.float32, 0.02, 0.0,
+                               rescale=True),
+}
+
+
+# ---------------------------------------------------------------------------------------------
+def timed_loop(wl, g16, steps, stream):
+    """Returns device milliseconds for `steps` consecutive steps (events on the launching stream)."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        wl.step(g16)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def run_ours(args, rank, world, dev):
+    import gtx16_fp16 as g16
+    from gtx16_fp16 import _native
+
+    peaks, peak_src = load_peaks()
+    wl = WORKLOADS[args.workload](dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        wl.step(g16)
+    torch.cuda.synchronize(dev)
+
+    sampler = ClockSampler(dev.index or 0)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    l0 = _native.launch_count()
+    with sampler:
+        ms = timed_loop(wl, g16, args.steps, stream)
+    torch.cuda.synchronize(dev)
+    launches = _native.launch_count() - l0
+    barrier(world)
+    ms_max = reduce_max(ms, world, dev)
+    ms_step = ms_max / args.steps
+
+    per_rank_units = wl.flops() / 1e12 if wl.unit == "TFLOPS" else wl.alg_bytes() / 1e9
+    value = world * per_rank_units / (ms_step * 1e-3)
+
+    # e2e through the public API with host buffers
+    hin, hout = wl.host_inputs(), wl.host_out()
+    for _ in range(max(2, args.warmup // 4)):
+        wl.e2e_step(g16, hin, hout)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_steps = max(3, min(args.steps, 50))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(e2e_steps):
+        wl.e2e_step(g16, hin, hout)
+    e.record(stream)
+    e.synchronize()
+    e2e_ms = reduce_max(s.elapsed_time(e), world, dev) / e2e_steps
+    h2d = sum(t.numel() * t.element_size() for t in hin)
+    d2h = hout.numel() * hout.element_size()
+
+    # roofline of the dominant kernel (the only libg16 kernel per step for fp16 GEMM workloads)
+    if wl.bound == "tensor":
+        peak = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        achieved = wl.flops() / (ms_step * 1e-3) / 1e12
+        unit = "TFLOP/s"
+    else:
+        peak = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+        achieved = wl.alg_bytes() / (ms_step * 1e-3) / 1e9
+        unit = "GB/s"
+    traffic = load_profile_traffic().get(args.workload)
+    roof = {"bound": wl.bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "peak_source": f"{peak_src} ({'bf16_tflops burst' if wl.bound == 'tensor' else 'hbm_gbs copy'})",
+            "basis": (f"2*M*N*K = {wl.flops():.4g} FLOP per launch" if wl.bound == "tensor" else
+                      f"2KN+xMK+4N+oMN = {wl.alg_bytes():.4g} B per launch"),
+            "launches_per_step": launches / max(args.steps, 1)}
+
+    line = {"metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
+            "config": dict(wl.config(), parallelism=f"replicas x{world}"),
+            "e2e": {"value": round(world * per_rank_units / (e2e_ms * 1e-3), 3), "unit": wl.unit,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms, 4), "api": "gtx16_fp16 public API, pinned host buffers"},
+            "roofline": roof, "gpu_launches": int(launches), "clocks": sampler.summary(), "impl": "ours"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(wl)
+    if rank == 0 and args.extra:
+        line["sub"] = sub_metrics(args, dev, g16, peaks)
+    return line
+
+
+def sub_metrics(args, dev, g16, peaks):
+    """Short measurements of the other BASELINE configs (same timing rules), for context."""
+    out = {}
+    for name in [n for n in args.extra.split(",") if n and n != args.workload]:
+        wl = WORKLOADS[name](dev)
+        for _ in range(5):
+            wl.step(g16)
+        torch.cuda.synchronize(dev)
+        steps = 50 if name != "gemm16384" else 10
+        ms = timed_loop(wl, g16, steps, torch.cuda.current_stream(dev)) / steps
+        if wl.unit == "TFLOPS":
+            v = wl.flops() / (ms * 1e-3) / 1e12
+            frac = v / peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        else:
+            v = wl.alg_bytes() / (ms * 1e-3) / 1e9
+            frac = v / peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+        out[name] = {"value": round(v, 2), "unit": wl.unit, "us_per_step": round(ms * 1e3, 2),
+                     "frac_of_measured_peak": round(frac, 4), "config": wl.config()}
+        del wl
+        torch.cuda.empty_cache()
+    return out
+
+
+def cpu_baseline(wl):
+    from oracle import cpu_path
+    cores = cpu_path.use_all_cores()
+    fn, units, sample = wl.cpu_sample()
+    fn()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        fn()
+        n += 1
+        if time.perf_counter() - t0 > 3.0 or n >= 20:
+            break
+    dt = (time.perf_counter() - t0) / n
+    if wl.unit == "TFLOPS":
+        v = units / dt / 1e12
+    else:  # GB/s of the same algorithmic bytes, scaled to the sample
+        v = wl.alg_bytes() * (units / wl.flops()) / dt / 1e9
+    return {"value": round(v, 5), "unit": wl.unit, "cores": cores, "kind": "port", "sample": sample,
+            "seconds_per_sample": round(dt, 4)}
+
+
+def run_reference(args, rank, world, dev):
+    """The reference's CPU implementation of the path (torch fp32 fallback) on the host cores."""
+    if rank != 0:
+        return None
+    from oracle import cpu_path
+    wl = WORKLOADS[args.workload](dev)
+    cores = cpu_path.use_all_cores()
+    fn, units, sample = wl.cpu_sample()
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    dt = (time.perf_counter() - t0) / args.steps
+    v = units / dt / 1e12 if wl.unit == "TFLOPS" else wl.alg_bytes() * (units / wl.flops()) / dt / 1e9
+    return {"metric": wl.metric, "value": round(v, 5), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "config": dict(wl.config(), parallelism="cpu"),
+            "impl": "reference",
+            "cpu_baseline": {"value": round(v, 5), "unit": wl.unit, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 5), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------------------------------------
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def reduce_max(v, world, dev):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="gemm4096", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--extra", default="skinny1,skinny4,skinny,splitk,splitk64,rescale",
+                    help="comma list of other workloads measured briefly into 'sub' (rank 0); '' to skip")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference" and rank != 0:
+        return  # the reference arm is the host CPU path: rank 0 alone runs and prints it
+    if world > 1 and args.impl == "ours":
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, rank, 1, dev)
+        else:
+            line = run_ours(args, rank, world, dev)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

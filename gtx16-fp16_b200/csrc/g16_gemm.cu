@@ -1,0 +1,469 @@
+// Tensor-core GEMM for the M > 8 path: out[M,N] = (A[M,K] @ B[K,N]) * rscale[row] + bias[col].
+//
+// Reference behaviour replaced: hgemm_body / hgemm_f32out / hgemm_f16out / hgemm_splitk
+// (src/gtx16_fp16/kernels.py:35-151) and the split-K host logic of mm_t (ops.py:92-107). The
+// reference is a 128x128 SIMT tile with packed-fp16 FMA over 16-wide K slices folded into fp32;
+// its split-K variant adds partial tiles into a prefilled fp32 output with atomics.
+//
+// B200 design (sm_100a):
+//   * persistent kernel, one CTA per SM, static round-robin over work units; a unit is one
+//     128x256 output tile (or one K chunk of it in split-K mode);
+//   * warp 0: TMA producer (one elected thread) filling a 4-stage shared-memory ring with 128-byte
+//     swizzled tiles: A [128 x 64] K-major, B [64 x 256] N-major (w_t is [K, N] row-major);
+//   * warp 1: allocates 512 TMEM columns (two 128x256 fp32 accumulators) and issues
+//     tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) from one thread; tcgen05.commit
+//     releases smem stages and publishes finished accumulators;
+//   * warps 2-5: epilogue; each reads its 32 TMEM lanes with tcgen05.ld, applies the per-row
+//     power-of-two unscale and fp32 bias, converts and stores, overlapping the next tile's MMAs;
+//   * split-K (few output tiles): each unit writes an fp32 partial tile to the workspace; the last
+//     unit to arrive on a tile (atomic counter, no waiting) sums the partials in split order and
+//     runs the same epilogue, then re-zeroes the counter. Results are bitwise reproducible.
+// Every wait is bounded; on expiry the kernel records G16_ERR_TIMEOUT in the device status word,
+// drains its in-flight copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "g16_internal.cuh"
+#include "g16_ptx.cuh"
+
+namespace g16 {
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kThreads = 192;  // 6 warps
+constexpr int kEpiThreads = 128;
+constexpr uint32_t kABytes = kBM * kBK * 2;     // 16 KiB
+constexpr uint32_t kBBoxBytes = kBK * 64 * 2;   // one [64 k x 64 n] box: 8 KiB
+constexpr uint32_t kBBytes = kBK * kBN * 2;     // 32 KiB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemCols = 2 * kBN;         // double-buffered accumulator
+constexpr int kGroupM = 8;                      // tile rasterisation: 8 tile-rows per group
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers etc.*/;
+
+struct GemmArgs {
+  void* out;
+  const float* bias;
+  const float* rscale;
+  float* partials;  // [tiles][ksplit][kBM][kBN] fp32 (split-K only)
+  int* counters;    // [tiles] (split-K only)
+  int* status;      // device status word
+  int M, N, K;
+  int m_tiles, n_tiles, tiles;
+  int ksplit, kblocks, kb_per_split, units;
+};
+
+struct Unit {
+  int tile, mt, nt, split, kb0, kb1;
+};
+
+__device__ __forceinline__ Unit unit_coords(const GemmArgs& a, int u) {
+  Unit r;
+  r.tile = u / a.ksplit;
+  r.split = u - r.tile * a.ksplit;
+  // Grouped rasterisation: walk kGroupM tile-rows together so B column panels stay in L2.
+  const int per_group = kGroupM * a.n_tiles;
+  const int g = r.tile / per_group;
+  const int first_m = g * kGroupM;
+  const int gsize = min(kGroupM, a.m_tiles - first_m);
+  const int in_g = r.tile - g * per_group;
+  r.mt = first_m + in_g % gsize;
+  r.nt = in_g / gsize;
+  r.kb0 = r.split * a.kb_per_split;
+  r.kb1 = min(a.kblocks, r.kb0 + a.kb_per_split);
+  return r;
+}
+
+__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void report_timeout(int* status, volatile int* abort_flag) {
+  *abort_flag = 1;
+  atomicExch(status, G16_ERR_TIMEOUT);
+}
+
+__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// Store 32 consecutive fp32 results (one row, columns col0..col0+31) with unscale and bias.
+template <bool OUT_F16>
+__device__ __forceinline__ void store_row32(const GemmArgs& a, int row, int col0, float rs, const float (&v)[32]) {
+  if (row >= a.M) return;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int col = col0 + 8 * g;
+    if (col >= a.N) break;  // N % 8 == 0: whole 8-column groups are in or out
+    float o[8];
+    if (a.bias != nullptr) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.bias + col));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.bias + col + 4));
+      o[0] = fmaf(v[8 * g + 0], rs, b0.x); o[1] = fmaf(v[8 * g + 1], rs, b0.y);
+      o[2] = fmaf(v[8 * g + 2], rs, b0.z); o[3] = fmaf(v[8 * g + 3], rs, b0.w);
+      o[4] = fmaf(v[8 * g + 4], rs, b1.x); o[5] = fmaf(v[8 * g + 5], rs, b1.y);
+      o[6] = fmaf(v[8 * g + 6], rs, b1.z); o[7] = fmaf(v[8 * g + 7], rs, b1.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[8 * g + j] * rs;
+    }
+    const size_t off = static_cast<size_t>(row) * a.N + col;
+    if constexpr (OUT_F16) {
+      __half2 h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) + off) = *reinterpret_cast<const uint4*>(h);
+    } else {
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + off);
+      dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+    }
+  }
+}
+
+template <bool OUT_F16>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+            const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* tfull_bar = empty_bar + kStages;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_base_slot + 2);
+  volatile int* stop_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], kEpiThreads / 32);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_phase[kStages];
+      bool armed[kStages];
+      for (int s = 0; s < kStages; ++s) { armed[s] = false; armed_phase[s] = 0; }
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+        const Unit w = unit_coords(args, u);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = stage_base + stage * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+          armed[stage] = true;
+          armed_phase[stage] = phase;
+          tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * kBK, w.mt * kBM);
+#pragma unroll
+          for (int j = 0; j < kBN / 64; ++j)
+            tma_load_2d(sb + j * kBBoxBytes, &tmap_b, &full_bar[stage], w.nt * kBN + 64 * j, kb * kBK);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        report_timeout(args.status, abort_flag);
+        // Drain: never leave the CTA with bulk copies still landing in its shared memory.
+        for (int s = 0; s < kStages; ++s)
+          if (armed[s]) mbar_wait(&full_bar[s], armed_phase[s], nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN, /*b_mn_major=*/true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+        const Unit w = unit_coords(args, u);
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(stage_base + stage * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // A: K-major, rows of 128 B, 8-row atoms 1024 B apart (SBO); step K by 32 B.
+            const uint64_t adesc = smem_desc_sw128(sa + k * (kUmmaK * 2), 16, 1024);
+            // B: N-major, 64-column blocks 8 KiB apart (LBO), 8-row k-groups 1024 B apart (SBO);
+            // step K by 16 rows of 128 B.
+            const uint64_t bdesc = smem_desc_sw128(sb + k * (kUmmaK * 128), kBBoxBytes, 1024);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb > w.kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      if (!ok) report_timeout(args.status, abort_flag);
+      // Wait for every issued MMA before TMEM is released.
+      umma_commit(drain_bar);
+      mbar_wait(drain_bar, 0, nullptr);
+    }
+  } else {
+    // ---------------- Epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int r_local = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
+      const Unit w = unit_coords(args, u);
+      // Every lane waits; the outcome is made warp-uniform (and the warp reconverged) before any
+      // .sync.aligned tcgen05 instruction.
+      bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag);
+      got = __all_sync(0xffffffffu, got);
+      if (!got && lane == 0) report_timeout(args.status, abort_flag);
+      const int row = w.mt * kBM + r_local;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+      if (args.ksplit == 1) {
+        if (!got) break;
+        tc_fence_after();
+        const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          store_row32<OUT_F16>(args, row, w.nt * kBN + c * 32, rs, v);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      } else {
+        // All four epilogue warps pass the same three named barriers per unit, even after a
+        // timeout, so none can be left waiting on a hardware barrier; they leave together.
+        if (got) {
+          tc_fence_after();
+          float* my_part = args.partials + (static_cast<size_t>(w.tile) * args.ksplit + w.split) * (kBM * kBN) +
+                           static_cast<size_t>(r_local) * kBN;
+#pragma unroll 1
+          for (int c = 0; c < kBN / 32; ++c) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(t_row + c * 32, r);
+            tmem_ld_wait();
+            float4* dst = reinterpret_cast<float4*>(my_part + c * 32);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        }
+        // Publish this partial, then count arrivals on the tile; the last arriver reduces.
+        __threadfence();
+        named_sync_epi();
+        if (threadIdx.x == 64) {
+          int last = 0;
+          if (!*abort_flag) {
+            const int prev = atomicAdd(args.counters + w.tile, 1);
+            last = (prev == args.ksplit - 1) ? 1 : 0;
+            if (last) args.counters[w.tile] = 0;  // every split has arrived: reset for the next call
+          }
+          *last_flag = last;
+          __threadfence();
+        }
+        named_sync_epi();
+        if (*last_flag) {
+          __threadfence();
+          const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
+          const float* base = args.partials + static_cast<size_t>(w.tile) * args.ksplit * (kBM * kBN) +
+                              static_cast<size_t>(r_local) * kBN;
+#pragma unroll 1
+          for (int c = 0; c < kBN / 32; ++c) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 t = ldcg4(base + c * 32 + 4 * j);
+              v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+            }
+            for (int s = 1; s < args.ksplit; ++s) {
+              const float* p = base + static_cast<size_t>(s) * (kBM * kBN) + c * 32;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 t = ldcg4(p + 4 * j);
+                v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+              }
+            }
+            store_row32<OUT_F16>(args, row, w.nt * kBN + c * 32, rs, v);
+          }
+        }
+        if (threadIdx.x == 64) *stop_flag = *abort_flag;
+        named_sync_epi();  // last_flag / stop_flag are reused by the next unit
+        if (*stop_flag) break;
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn(int* status) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (fn == nullptr) *status = err != cudaSuccess ? cuda_fail(err) : G16_ERR_CUDA;
+  return fn;
+}
+
+// 2-D fp16 tensor map over a row-major [rows, cols] matrix with a [box_rows, 64] box and 128-byte
+// swizzle (64 fp16 = 128 bytes per box row).
+int make_tmap_fp16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  int st = G16_OK;
+  auto fn = encode_fn(&st);
+  if (fn == nullptr) return st;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? G16_OK : G16_ERR_CUDA;
+}
+
+size_t partial_bytes(int tiles, int ksplit) {
+  return static_cast<size_t>(tiles) * ksplit * kBM * kBN * sizeof(float);
+}
+
+int tiles_of(int M, int N) { return ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN); }
+
+}  // namespace
+
+int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev) {
+  const int tiles = tiles_of(M, N);
+  const int kblocks = (K + kBK - 1) / kBK;
+  if (tiles * 2 > dev.sm_count || kblocks < 8) return 1;
+  int ks = dev.sm_count / tiles;
+  const int by_k = kblocks / 4;  // keep at least 4 k-blocks (256 of K) per split
+  if (ks > by_k) ks = by_k;
+  if (tiles * 4 > static_cast<int>(kCounterBytes)) return 1;
+  return ks < 1 ? 1 : ks;
+}
+
+size_t gemm_workspace_bytes(int M, int K, int N, int ksplit) {
+  if (ksplit <= 1) return 0;
+  (void)K;
+  return kCounterBytes + partial_bytes(tiles_of(M, N), ksplit);
+}
+
+int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                const float* rscale, int M, int K, int N, int ksplit, void* ws, size_t ws_bytes, cudaStream_t s,
+                const DeviceInfo& dev) {
+  if (M <= 0 || N <= 0) return G16_OK;
+  const int kblocks = (K + kBK - 1) / kBK;
+  if (ksplit < 1) ksplit = 1;
+  if (ksplit > kblocks) ksplit = kblocks;
+  GemmArgs args{};
+  args.out = out;
+  args.bias = bias;
+  args.rscale = rscale;
+  args.status = device_status_ptr();
+  if (args.status == nullptr) return G16_ERR_CUDA;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.m_tiles = (M + kBM - 1) / kBM;
+  args.n_tiles = (N + kBN - 1) / kBN;
+  args.tiles = args.m_tiles * args.n_tiles;
+  args.kblocks = kblocks;
+  args.kb_per_split = (kblocks + ksplit - 1) / ksplit;
+  ksplit = (kblocks + args.kb_per_split - 1) / args.kb_per_split;  // no empty splits
+  args.ksplit = ksplit;
+  args.units = args.tiles * ksplit;
+  if (ksplit > 1) {
+    if (args.tiles * 4 > static_cast<int>(kCounterBytes)) return G16_ERR_ARG;
+    const size_t need = kCounterBytes + partial_bytes(args.tiles, ksplit);
+    if (ws == nullptr || ws_bytes < need) return G16_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return G16_ERR_ALIGN;
+    args.counters = static_cast<int*>(ws);
+    args.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
+  }
+
+  CUtensorMap ta, tb;
+  int st = make_tmap_fp16(&ta, a16, static_cast<uint64_t>(M), static_cast<uint64_t>(K), kBM);
+  if (st != G16_OK) return st;
+  st = make_tmap_fp16(&tb, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N), kBK);
+  if (st != G16_OK) return st;
+
+  const int grid = args.units < dev.sm_count ? args.units : dev.sm_count;
+  cudaError_t e;
+  if (out_dtype == G16_F16) {
+    e = cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return cuda_fail(e);
+    gemm_kernel<true><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
+  } else {
+    e = cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return cuda_fail(e);
+    gemm_kernel<false><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  note_launch();
+  return G16_OK;
+}
+
+}  // namespace g16

@@ -1,0 +1,55 @@
+// Internal declarations shared by the kernel translation units and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/g16.h"
+
+namespace g16 {
+
+// Device status word (G16_OK or G16_ERR_TIMEOUT), one per device, defined in g16_api.cu.
+// Kernels compiled in other translation units receive its address as a parameter.
+int* device_status_ptr();  // host: device address of the current device's status word
+
+// Records the CUDA error and returns G16_ERR_CUDA (host).
+int cuda_fail(cudaError_t e);
+
+// Per-device facts cached on first use (host).
+struct DeviceInfo {
+  int sm_count = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+  int max_smem_optin = 0;
+};
+const DeviceInfo* device_info(int* status);  // current device; nullptr + status on failure
+
+void note_launch(uint64_t n = 1);
+
+// ---- launchers (host), each returns a g16_status code ----
+int launch_skinny(const void* x, int x_dtype, const uint16_t* w, const float* bias, void* out, int out_dtype, int M,
+                  int K, int N, cudaStream_t s, const DeviceInfo& dev);
+
+int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M, int K, float thresh,
+                    cudaStream_t s);
+
+// Tensor-core GEMM. ws must hold gemm_workspace_bytes(M, K, N, ksplit) when ksplit > 1.
+int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                const float* rscale, int M, int K, int N, int ksplit, void* ws, size_t ws_bytes, cudaStream_t s,
+                const DeviceInfo& dev);
+size_t gemm_workspace_bytes(int M, int K, int N, int ksplit);
+int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// GEMM tile geometry (also used for workspace sizing on the host).
+constexpr int kBM = 128;   // UMMA M (one CTA, cta_group::1)
+constexpr int kBN = 256;   // UMMA N
+constexpr int kBK = 64;    // K per pipeline stage: one 128-byte swizzle row of fp16
+constexpr int kUmmaK = 16; // K per tcgen05.mma for 16-bit inputs
+
+// Split-K workspace layout: [kCounterBytes of per-tile arrival counters][partials fp32].
+constexpr size_t kCounterBytes = 4096;
+
+}  // namespace g16

@@ -1,0 +1,141 @@
+// Per-row overflow rescale before the fp16 cast of the GEMM path.
+//
+// Reference behaviour replaced: rowscale_body / rowscale_f32 / rowscale_f16
+// (src/gtx16_fp16/kernels.py:227-250), launched by mm_t for every M > 8 call (ops.py:86-90):
+//   amax = max_k |x[row,k]|
+//   S[row] = 2^ceil(log2(amax / thresh)) if amax > thresh else 1
+//   y[row,k] = fp16_rn(x[row,k] / S[row])
+// The reference evaluates the exponent with fast-math log2f/exp2f; here ceil(log2(r)) is read
+// exactly from the IEEE-754 exponent and mantissa fields of r = amax / thresh (no transcendental
+// call), so S is always the smallest power of two with amax / S <= thresh.
+//
+// One CTA per row; the row is read from HBM once (the second pass hits L1/L2) and written once.
+#include <cuda_fp16.h>
+
+#include "g16_internal.cuh"
+#include "g16_ptx.cuh"
+
+namespace g16 {
+namespace {
+
+constexpr int kThreads = 256;
+
+// Smallest power of two S with amax / S <= thresh (S = 1 when amax <= thresh). Returns the
+// scale and writes its exact reciprocal.
+__device__ __forceinline__ float pow2_row_scale(float amax, float thresh, float* inv) {
+  if (!(amax > thresh)) {
+    *inv = 1.f;
+    return 1.f;
+  }
+  const float r = amax / thresh;  // exact when thresh is a power of two
+  const uint32_t b = __float_as_uint(r);
+  const int e = static_cast<int>((b >> 23) & 0xFFu);
+  if (e == 0xFF) {  // amax = inf: the reference's exp2f(inf) gives S = inf, 1/S = 0
+    *inv = 0.f;
+    return __uint_as_float(0x7F800000u);
+  }
+  // r >= 1 here, so r is a normal number: log2(r) = (e - 127) + log2(1.mantissa).
+  const int c = (e - 127) + ((b & 0x7FFFFFu) != 0u ? 1 : 0);  // ceil(log2(r)), 0 <= c <= 128
+  if (c >= 128) {
+    *inv = 0.f;
+    return __uint_as_float(0x7F800000u);
+  }
+  *inv = __uint_as_float(static_cast<uint32_t>(127 - c) << 23);  // 2^-c, normal for c <= 126
+  return __uint_as_float(static_cast<uint32_t>(127 + c) << 23);  // 2^c
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int i = 1; i < kThreads / 32; ++i) r = fmaxf(r, red[i]);
+  return r;
+}
+
+// K % 8 == 0 and 16-byte aligned rows (K % 8 == 0 with a 16-byte aligned base) are required.
+__global__ void __launch_bounds__(kThreads) rowscale_f32_kernel(const float* __restrict__ x, __half* __restrict__ y,
+                                                                float* __restrict__ S, int K, float thresh) {
+  __shared__ float red[kThreads / 32];
+  const size_t row = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * K);
+  const int nv = K / 4;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < nv; i += kThreads) {
+    const float4 v = xr[i];
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  const float amax = block_max(m, red);
+  float inv;
+  const float sc = pow2_row_scale(amax, thresh, &inv);
+  uint2* yr = reinterpret_cast<uint2*>(y + row * K);
+  for (int i = threadIdx.x; i < nv; i += kThreads) {
+    float4 v = xr[i];
+    if (sc != 1.f) { v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv; }
+    const __half2 h0 = __floats2half2_rn(v.x, v.y);
+    const __half2 h1 = __floats2half2_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&h0);
+    o.y = *reinterpret_cast<const uint32_t*>(&h1);
+    yr[i] = o;
+  }
+  if (threadIdx.x == 0) S[row] = sc;
+}
+
+__global__ void __launch_bounds__(kThreads) rowscale_f16_kernel(const __half* __restrict__ x, __half* __restrict__ y,
+                                                                float* __restrict__ S, int K, float thresh) {
+  __shared__ float red[kThreads / 32];
+  const size_t row = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
+  const int nv = K / 8;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < nv; i += kThreads) {
+    const uint4 v = xr[i];
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  const float amax = block_max(m, red);
+  float inv;
+  const float sc = pow2_row_scale(amax, thresh, &inv);
+  uint4* yr = reinterpret_cast<uint4*>(y + row * K);
+  for (int i = threadIdx.x; i < nv; i += kThreads) {
+    uint4 v = xr[i];
+    if (sc != 1.f) {
+      __half2* h = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        h[j] = __floats2half2_rn(f.x * inv, f.y * inv);
+      }
+    }
+    yr[i] = v;
+  }
+  if (threadIdx.x == 0) S[row] = sc;
+}
+
+}  // namespace
+
+int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M, int K, float thresh,
+                    cudaStream_t s) {
+  if (M <= 0) return G16_OK;
+  if (x_dtype == G16_F32) {
+    rowscale_f32_kernel<<<M, kThreads, 0, s>>>(static_cast<const float*>(x), reinterpret_cast<__half*>(y16), rscale,
+                                                K, thresh);
+  } else {
+    rowscale_f16_kernel<<<M, kThreads, 0, s>>>(static_cast<const __half*>(x), reinterpret_cast<__half*>(y16),
+                                                rscale, K, thresh);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  note_launch();
+  return G16_OK;
+}
+
+}  // namespace g16

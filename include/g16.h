@@ -1,0 +1,119 @@
+/*
+ * g16.h - C ABI of the B200 (sm_100a) fp16 matmul hot path.
+ *
+ * Drop-in for the kernel layer of gtx16_fp16: the reference compiles seven CUDA C kernels with
+ * NVRTC and launches them through ctypes cuLaunchKernel (src/gtx16_fp16/kernels.py:299-338).
+ * This library replaces that layer with hand-written sm_100a kernels behind plain C entry points:
+ * raw device pointers, int sizes, a dtype code and the caller's cudaStream_t passed as void*.
+ *
+ * Ownership: the caller owns every buffer (inputs, output, workspace). The library never
+ * allocates, frees or synchronises; inputs are never written. All work is enqueued on `stream`
+ * on the current CUDA device. Every entry point returns a g16_status code; none throws.
+ *
+ * Numerics (all paths): fp32 accumulation. GEMM path: fp16 x fp16 products on the tcgen05
+ * tensor cores; fp32 activations are first cast to fp16 with the reference's per-row
+ * power-of-two overflow rescale (rows with |max| > thresh). Skinny path (M <= 8): fp32 FMA of the
+ * fp32/fp16 activations against fp16 weights. Results are bitwise reproducible run to run on the
+ * same device (no floating-point atomics).
+ */
+#ifndef G16_H
+#define G16_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type codes (the reference accepts exactly these two, src/gtx16_fp16/ops.py:29-35,70-71). */
+enum g16_dtype { G16_F32 = 0, G16_F16 = 1 };
+
+enum g16_status {
+  G16_OK = 0,
+  G16_ERR_ARG = 1,         /* bad size, dtype code or null pointer                               */
+  G16_ERR_UNSUPPORTED = 2, /* shape outside the gate of ops.py:29-35 (K % 8, N % 8)              */
+  G16_ERR_ALIGN = 3,       /* a pointer is not 16-byte aligned                                    */
+  G16_ERR_WORKSPACE = 4,   /* workspace missing or smaller than g16_mm_t_workspace_bytes()        */
+  G16_ERR_CUDA = 5,        /* a CUDA runtime call failed; see g16_last_cuda_error()               */
+  G16_ERR_DEVICE = 6,      /* the current device is not sm_100 (B200-class)                       */
+  G16_ERR_TIMEOUT = 7      /* a kernel's bounded device-side wait expired (pipeline fault)        */
+};
+
+/* Largest M served by the skinny (GEMV) path: SKINNY_MAX_M, src/gtx16_fp16/kernels.py:253. */
+#define G16_SKINNY_MAX_M 8
+/* Rows whose |max| exceeds this are scaled by a power of two before the fp16 cast:
+ * ROW_SCALE_THRESHOLD, src/gtx16_fp16/ops.py:14-16. */
+#define G16_ROW_SCALE_THRESHOLD 1024.0f
+
+/*
+ * out[M,N] = x[M,K] @ w_t[K,N] + bias[N], dispatched like the reference's mm_t
+ * (src/gtx16_fp16/ops.py:65-108): M <= 8 -> skinny GEMV; otherwise rowscale (fp32 x only) and the
+ * tensor-core GEMM, with a deterministic split-K reduction when the output has too few tiles to
+ * fill the GPU (replaces hgemm_splitk's fp32 atomics, ops.py:92-101).
+ *   x        [M,K] row-major, dtype x_dtype (G16_F32 or G16_F16), 16-byte aligned
+ *   w_t      [K,N] row-major fp16, 16-byte aligned
+ *   bias     [N] fp32 or NULL
+ *   out      [M,N] row-major, dtype out_dtype, 16-byte aligned, must not alias any input
+ *   workspace/workspace_bytes: scratch of at least g16_mm_t_workspace_bytes(M,K,N,x_dtype);
+ *            its first 4 KiB must be zero before the first call and are left zero by every call
+ *            that completes; may be NULL when that size is 0.
+ * Requires K % 8 == 0, N % 8 == 0, M >= 0 (M == 0 is a no-op).
+ */
+int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, void* out, int out_dtype, int M, int K,
+             int N, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace g16_mm_t needs for this problem on the current device (0 when none). */
+size_t g16_mm_t_workspace_bytes(int M, int K, int N, int x_dtype);
+
+/*
+ * Skinny path alone, M in [1, 8]: out[M,N] = x[M,K] @ w_t[K,N] + bias (fp32 accumulate).
+ * Replaces skinny_f32in / skinny_f16in (src/gtx16_fp16/kernels.py:163-219) plus the zero-fill and
+ * fp16 cast around them (ops.py:78-84). K is split across the CTAs of a thread-block cluster and
+ * reduced in a fixed order through distributed shared memory, so no zeroed output is needed.
+ */
+int g16_skinny(const void* x, int x_dtype, const uint16_t* w_t, const float* bias, void* out, int out_dtype, int M,
+               int K, int N, void* stream);
+
+/*
+ * Per-row overflow rescale: S[row] = 2^ceil(log2(amax/thresh)) if amax > thresh else 1;
+ * y16 = fp16(x / S). Replaces rowscale_f32 / rowscale_f16 (src/gtx16_fp16/kernels.py:227-250).
+ */
+int g16_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M, int K, float thresh, void* stream);
+
+/*
+ * Tensor-core GEMM: out[M,N] = (a16[M,K] @ b16[K,N]) * rscale[row] + bias[col], fp32 accumulate in
+ * TMEM, fused epilogue. Replaces hgemm_f32out / hgemm_f16out / hgemm_splitk
+ * (src/gtx16_fp16/kernels.py:139-151). rscale and bias may be NULL. ksplit = 0 picks the split
+ * automatically; ksplit = 1 forces a single pass; ksplit > 1 forces that many K chunks (the
+ * workspace must then hold g16_gemm_workspace_bytes(M,K,N,ksplit)).
+ */
+int g16_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+             const float* rscale, int M, int K, int N, int ksplit, void* workspace, size_t workspace_bytes,
+             void* stream);
+
+/* Workspace bytes for g16_gemm with the given ksplit (0 = automatic choice). */
+size_t g16_gemm_workspace_bytes(int M, int K, int N, int ksplit);
+
+/* The K-split g16_gemm would choose automatically for this shape on the current device. */
+int g16_gemm_auto_ksplit(int M, int K, int N);
+
+/* Device-side status word of the current device: G16_OK, or G16_ERR_TIMEOUT if a kernel's
+ * bounded wait expired since the last clear. Synchronises `stream`. clear != 0 resets it. */
+int g16_device_status(int* status_out, int clear, void* stream);
+
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t g16_launch_count(void);
+
+/* Human-readable text for a g16_status code; the last CUDA error text for G16_ERR_CUDA. */
+const char* g16_strerror(int status);
+int g16_last_cuda_error(void);
+
+/* Library ABI version (major * 10000 + minor * 100 + patch). */
+int g16_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* G16_H */

@@ -1,0 +1,234 @@
+"""GPU parity of the sm_100a kernels: the reference's test suite (tests/test_correctness.py) ported to
+this package, with the fp64 product as ground truth and the tolerances of tests/_tol.py, plus bitwise
+determinism, forced split-K, the C ABI called directly, and the native-path-was-used check."""
+import ctypes
+
+import pytest
+import torch
+import torch.nn as nn
+
+import gtx16_fp16 as g
+from gtx16_fp16 import _native
+
+from _tol import GEMM_NORM, assert_close_fp64, ref64, rel_err
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [  # (M, K, N): tile-aligned, ragged edges, skinny (M <= 8), tiny (tests/test_correctness.py:14-18)
+    (128, 128, 128), (256, 512, 384), (1000, 1032, 776), (129, 136, 8), (3, 4096, 4096),
+    (1, 1024, 3072), (8, 2048, 520), (9, 64, 64), (4096, 4096, 1024), (17, 8, 4104),
+    (64, 1024, 1024), (33, 4096, 768), (200, 1032, 136),  # split-K path
+]
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_mm_t_matches_fp64(cuda_ok, M, K, N, out_dtype, with_bias):
+    torch.manual_seed(M * 7 + K * 3 + N)
+    x = (torch.randn(M, K, device="cuda") * 0.5).half()
+    w = (torch.randn(K, N, device="cuda") * 0.5).half()
+    b = torch.randn(N, device="cuda") if with_bias else None
+    assert g.supported(x, w)
+    y = g.mm_t(x, w, b, out_dtype)
+    assert y.dtype == out_dtype and y.shape == (M, N)
+    assert_close_fp64(y, x, w, b, out_dtype, f"{M}x{K}x{N}")
+    # the reference's own bound against an fp32 reference (tests/test_correctness.py:35)
+    assert rel_err(y, x.float() @ w.float() + (b if with_bias else 0)) < (2e-3 if out_dtype == torch.float16 else 1.5e-3)
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 64, 300])
+def test_fp32_activations_match_fp64(cuda_ok, M):
+    torch.manual_seed(M)
+    K, N = 1024, 768
+    x = torch.randn(M, K, device="cuda")
+    w = (torch.randn(K, N, device="cuda") * 0.05).half()
+    b = torch.randn(N, device="cuda") * 0.1
+    y = g.mm_t(x, w, b, torch.float32)
+    assert_close_fp64(y, x, w, b, torch.float32, f"fp32 x M={M}")
+
+
+@pytest.mark.parametrize("M", [1, 2, 8, 64, 1000])
+def test_bias_and_inputs_are_not_modified(cuda_ok, M):
+    x = torch.randn(M, 512, device="cuda").half()
+    w = torch.randn(512, 768, device="cuda").half()
+    b = torch.randn(768, device="cuda")
+    x0, w0, b0 = x.clone(), w.clone(), b.clone()
+    for _ in range(3):
+        g.mm_t(x, w, b, torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(x, x0) and torch.equal(w, w0) and torch.equal(b, b0)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 768), (8, 4096, 4096), (64, 1024, 1024), (128, 16384, 1024),
+                                   (1000, 1032, 776), (2048, 3072, 1024)])
+@pytest.mark.parametrize("xdt", [torch.float32, torch.float16])
+def test_bitwise_deterministic(cuda_ok, M, K, N, xdt):
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device="cuda").to(xdt)
+    w = (torch.randn(K, N, device="cuda") * 0.02).half()
+    b = torch.randn(N, device="cuda")
+    outs = [g.mm_t(x, w, b, torch.float32) for _ in range(4)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+
+
+def test_fast_linear_is_deterministic_across_calls(cuda_ok):
+    lin = nn.Linear(1024, 768).cuda()
+    fl = g.FastLinear.from_linear(lin)
+    x = torch.randn(1, 1024, device="cuda")
+    with torch.no_grad():
+        outs = [fl(x) for _ in range(4)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])  # stronger than the reference's rel < 1e-6
+
+
+def test_matmul_fallback_for_odd_shapes(cuda_ok):
+    a = torch.randn(33, 13, device="cuda").half()  # K % 8 != 0 -> torch fallback
+    b = torch.randn(13, 7, device="cuda").half()
+    assert not g.supported(a, b)
+    torch.testing.assert_close(g.matmul(a, b), (a @ b), rtol=1e-2, atol=1e-2)
+
+
+def test_matmul_uses_native_kernels(cuda_ok):
+    a = torch.randn(256, 512, device="cuda").half()
+    b = (torch.randn(512, 384, device="cuda") * 0.05).half()
+    before = _native.launch_count()
+    y = g.matmul(a, b)
+    torch.cuda.synchronize()
+    assert _native.launch_count() > before
+    assert y.dtype == torch.float16
+    assert_close_fp64(y, a, b, None, torch.float16, "matmul")
+
+
+def test_fast_linear_matches_nn_linear(cuda_ok):
+    torch.manual_seed(0)
+    lin = nn.Linear(1024, 768).cuda()
+    fl = g.FastLinear.from_linear(lin)
+    for shape in [(4, 50, 1024), (1, 1, 1024), (2, 1024), (7, 1024)]:
+        x = torch.randn(*shape, device="cuda")
+        with torch.no_grad():
+            ref, y = lin(x), fl(x)
+        assert y.dtype == torch.float32 and y.shape == ref.shape
+        assert rel_err(y, ref) < 3e-3
+
+
+def test_fast_linear_fp16_input_gives_fp16(cuda_ok):
+    lin = nn.Linear(512, 256).cuda()
+    fl = g.FastLinear.from_linear(lin)
+    x = torch.randn(3, 20, 512, device="cuda").half()
+    with torch.no_grad():
+        y = fl(x)
+    assert y.dtype == torch.float16 and y.shape == (3, 20, 256)
+    assert rel_err(y, lin(x.float())) < 3e-3
+
+
+def test_fast_linear_falls_back_when_grad_needed(cuda_ok):
+    lin = nn.Linear(256, 256).cuda()
+    fl = g.FastLinear.from_linear(lin)
+    x = torch.randn(4, 256, device="cuda", requires_grad=True)
+    fl(x).sum().backward()
+    assert x.grad is not None
+
+
+def test_patch_replaces_linear_layers(cuda_ok):
+    torch.manual_seed(0)
+    model = nn.Sequential(nn.Linear(512, 1024), nn.GELU(), nn.Linear(1024, 512), nn.Linear(512, 10)).cuda().eval()
+    x = torch.randn(64, 512, device="cuda")
+    with torch.no_grad():
+        ref = model(x)
+    assert g.patch(model, min_features=256) == 0  # B200 is not an affected GPU
+    n = g.patch(model, min_features=256, force=True)
+    assert n == 2  # the 512->10 head is below min_features
+    assert isinstance(model[0], g.FastLinear) and isinstance(model[3], nn.Linear)
+    with torch.no_grad():
+        y = model(x)
+    assert rel_err(y, ref) < 3e-3
+
+
+def test_patch_skip(cuda_ok):
+    model = nn.Sequential(nn.Linear(512, 512), nn.Linear(512, 512)).cuda()
+    assert g.patch(model, force=True, skip=("1",)) == 1
+    assert isinstance(model[0], g.FastLinear) and isinstance(model[1], nn.Linear)
+
+
+def test_large_outputs_do_not_overflow_with_fp32_out(cuda_ok):
+    x = torch.full((128, 4096), 16.0, device="cuda").half()
+    w = torch.full((4096, 128), 16.0, device="cuda").half()
+    y = g.mm_t(x, w, None, torch.float32)
+    assert torch.isfinite(y).all()
+    assert torch.all(y == 16 * 16 * 4096)  # exact in fp32 accumulation
+
+
+@pytest.mark.parametrize("M", [1, 5, 64, 300])
+@pytest.mark.parametrize("in_dtype", [torch.float32, torch.float16])
+def test_massive_activations_do_not_overflow(cuda_ok, M, in_dtype):
+    torch.manual_seed(1)
+    K, N = 3072, 1024
+    x = torch.randn(M, K, device="cuda")
+    x[:, 7] = 179940.0 if in_dtype == torch.float32 else 60000.0
+    x[0, 100] = -120000.0 if in_dtype == torch.float32 else -50000.0
+    x = x.to(in_dtype)
+    w = (torch.randn(K, N, device="cuda") * 0.3).half()
+    y = g.mm_t(x, w, None, torch.float32)
+    assert torch.isfinite(y).all()
+    assert rel_err(y, x.float() @ w.float()) < 2e-3
+    assert rel_err(y, ref64(x, w)) < GEMM_NORM
+
+
+def test_is_affected_reports_bool(cuda_ok):
+    assert isinstance(g.is_affected(), bool)
+    assert g.is_affected() is False  # sm_100
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 1024, 1024), (128, 16384, 1024), (300, 4096, 256), (129, 2048, 8)])
+@pytest.mark.parametrize("ksplit", [1, 2, 3, 7, 16])
+def test_forced_split_k_through_c_abi(cuda_ok, M, K, N, ksplit):
+    """g16_gemm with a forced K split: deterministic last-arriver reduction matches fp64."""
+    torch.manual_seed(ksplit)
+    a = torch.randn(M, K, device="cuda").half()
+    b = (torch.randn(K, N, device="cuda") * K ** -0.5).half()
+    bias = torch.randn(N, device="cuda")
+    L = _native.lib()
+    stream = _native.stream_handle(0)
+    nws = int(L.g16_gemm_workspace_bytes(M, K, N, ksplit))
+    ws = torch.zeros(max(nws, 1), dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(2):
+        out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+        st = L.g16_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), _native.G16_F32, bias.data_ptr(), None, M, K, N,
+                        ksplit, ws.data_ptr() if nws else None, nws, stream)
+        assert st == 0, _native.strerror(st)
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    assert_close_fp64(outs[0], a, b, bias, torch.float32, f"split {ksplit}")
+    if nws:  # counters are left at zero for the next call
+        assert int(ws[:4096].count_nonzero()) == 0
+
+
+def test_rowscale_through_c_abi(cuda_ok):
+    torch.manual_seed(5)
+    M, K = 64, 1024
+    x = torch.randn(M, K, device="cuda")
+    x[3, 11] = 179940.0
+    x[7, 0] = -2048.0
+    x[9, 5] = 1024.0
+    y = torch.empty(M, K, device="cuda", dtype=torch.float16)
+    S = torch.empty(M, device="cuda")
+    L = _native.lib()
+    st = L.g16_rowscale(x.data_ptr(), _native.G16_F32, y.data_ptr(), S.data_ptr(), M, K, 1024.0, _native.stream_handle(0))
+    assert st == 0
+    assert S[3].item() == 256.0 and S[7].item() == 2.0 and S[9].item() == 1.0 and S[0].item() == 1.0
+    torch.testing.assert_close(y.float(), (x / S[:, None]).half().float(), rtol=0, atol=0)
+
+
+def test_k_zero_gives_bias(cuda_ok):
+    x = torch.empty(16, 0, device="cuda").half()
+    w = torch.empty(0, 64, device="cuda").half()
+    b = torch.randn(64, device="cuda")
+    y = g.mm_t(x, w, b, torch.float32)
+    assert torch.equal(y, b.expand(16, 64))
+
+
+def test_device_status_clean_after_suite(cuda_ok):
+    assert _native.device_status(clear=False) == _native.OK
