@@ -291,15 +291,39 @@ WORKLOADS = {
 
 
 # ---------------------------------------------------------------------------------------------
-def timed_loop(wl, g16, steps, stream):
-    """Returns device milliseconds for `steps` consecutive steps (events on the launching stream)."""
+def timed_loop(wl, g16, steps, stream, graph=None):
+    """Device milliseconds for `steps` consecutive steps, CUDA events on the launching stream.
+
+    With `graph` (a CUDA graph holding exactly `steps` captured steps) the steps are replayed from
+    the graph, so host launch overhead does not stretch microsecond-scale steps."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    for _ in range(steps):
-        wl.step(g16)
+    if graph is not None:
+        graph.replay()
+    else:
+        for _ in range(steps):
+            wl.step(g16)
     end.record(stream)
     end.synchronize()
     return start.elapsed_time(end)
+
+
+def capture_steps(wl, g16, steps, stream):
+    """(graph, launches): a CUDA graph of `steps` consecutive steps captured on `stream` (warmed up
+    on it first) and the number of libg16 kernel launches it holds."""
+    from gtx16_fp16 import _native
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            wl.step(g16)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    l0 = _native.launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(steps):
+            wl.step(g16)
+    launches = _native.launch_count() - l0
+    stream.synchronize()
+    return graph, launches
 
 
 def run_ours(args, rank, world, dev):
@@ -312,15 +336,24 @@ def run_ours(args, rank, world, dev):
     for _ in range(args.warmup):
         wl.step(g16)
     torch.cuda.synchronize(dev)
+    graph = None
+    if args.graph:
+        gstream = torch.cuda.Stream(dev)
+        graph, launches = capture_steps(wl, g16, args.steps, gstream)
+        stream = gstream
+        graph.replay()  # one untimed replay: the warm-up of the captured work
+        torch.cuda.synchronize(dev)
 
     sampler = ClockSampler(dev.index or 0)
     barrier(world)
     torch.cuda.synchronize(dev)
-    l0 = _native.launch_count()
+    if graph is None:
+        l0 = _native.launch_count()
     with sampler:
-        ms = timed_loop(wl, g16, args.steps, stream)
+        ms = timed_loop(wl, g16, args.steps, stream, graph)
     torch.cuda.synchronize(dev)
-    launches = _native.launch_count() - l0
+    if graph is None:
+        launches = _native.launch_count() - l0
     barrier(world)
     ms_max = reduce_max(ms, world, dev)
     ms_step = ms_max / args.steps
@@ -329,6 +362,7 @@ def run_ours(args, rank, world, dev):
     value = world * per_rank_units / (ms_step * 1e-3)
 
     # e2e through the public API with host buffers
+    stream = torch.cuda.current_stream(dev)
     hin, hout = wl.host_inputs(), wl.host_out()
     for _ in range(max(2, args.warmup // 4)):
         wl.e2e_step(g16, hin, hout)
@@ -369,7 +403,8 @@ def run_ours(args, rank, world, dev):
             "e2e": {"value": round(world * per_rank_units / (e2e_ms * 1e-3), 3), "unit": wl.unit,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms, 4), "api": "gtx16_fp16 public API, pinned host buffers"},
-            "roofline": roof, "gpu_launches": int(launches), "clocks": sampler.summary(), "impl": "ours"}
+            "roofline": roof, "gpu_launches": int(launches), "clocks": sampler.summary(), "impl": "ours",
+            "timing": "CUDA graph of the K steps, replayed once" if graph is not None else "eager launches"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl)
     if rank == 0 and args.extra:
@@ -386,7 +421,13 @@ def sub_metrics(args, dev, g16, peaks):
             wl.step(g16)
         torch.cuda.synchronize(dev)
         steps = 50 if name != "gemm16384" else 10
-        ms = timed_loop(wl, g16, steps, torch.cuda.current_stream(dev)) / steps
+        graph, stream = None, torch.cuda.current_stream(dev)
+        if args.graph:
+            stream = torch.cuda.Stream(dev)
+            graph, _ = capture_steps(wl, g16, steps, stream)
+            graph.replay()
+            torch.cuda.synchronize(dev)
+        ms = timed_loop(wl, g16, steps, stream, graph) / steps
         if wl.unit == "TFLOPS":
             v = wl.flops() / (ms * 1e-3) / 1e12
             frac = v / peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
@@ -470,6 +511,7 @@ def main():
     ap.add_argument("--extra", default="skinny1,skinny4,skinny,splitk,splitk64,rescale",
                     help="comma list of other workloads measured briefly into 'sub' (rank 0); '' to skip")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", type=int, default=1, help="1: time a CUDA graph of the K steps (default); 0: eager")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

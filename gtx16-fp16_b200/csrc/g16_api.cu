@@ -45,9 +45,9 @@ int current_device(int* dev) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Workspace layout of g16_mm_t: [kCounterBytes counters | split-K partials | x16 | rscale].
+// Workspace layout of g16_mm_t: [split-K partials | x16 | rscale], each part 256-byte aligned.
 struct MmLayout {
-  size_t partials_off = 0, x16_off = 0, rscale_off = 0, total = 0;
+  size_t partials_bytes = 0, x16_off = 0, rscale_off = 0, total = 0;
   int ksplit = 1;
 };
 
@@ -55,16 +55,18 @@ MmLayout mm_layout(int M, int K, int N, int x_dtype, const DeviceInfo& dev) {
   MmLayout L;
   if (M <= G16_SKINNY_MAX_M || K == 0) return L;
   L.ksplit = gemm_auto_ksplit(M, K, N, dev);
-  size_t off = kCounterBytes;
-  L.partials_off = off;
-  if (L.ksplit > 1) off += align_up(gemm_workspace_bytes(M, K, N, L.ksplit) - kCounterBytes, 256);
+  size_t off = 0;
+  if (L.ksplit > 1) {
+    L.partials_bytes = align_up(gemm_workspace_bytes(M, K, N, L.ksplit), 256);
+    off += L.partials_bytes;
+  }
   if (x_dtype == G16_F32) {
     L.x16_off = off;
     off += align_up(static_cast<size_t>(M) * K * 2, 256);
     L.rscale_off = off;
     off += align_up(static_cast<size_t>(M) * 4, 256);
   }
-  L.total = off == kCounterBytes && L.ksplit <= 1 ? 0 : off;
+  L.total = off;
   return L;
 }
 
@@ -219,10 +221,8 @@ int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, voi
   }
   // fp16 activations need no rescale here: products accumulate in fp32 TMEM and cannot overflow
   // the way the reference's fp16 partial sums could.
-  // The split-K region is [0, x16_off) when x16 follows it, else the whole layout.
-  const size_t split_bytes = L.ksplit > 1 ? (L.x16_off > 0 ? L.x16_off : L.total) : 0;
   return launch_gemm(a16, static_cast<const uint16_t*>(w_t), out, out_dtype, bias, rscale, M, K, N, L.ksplit,
-                     L.ksplit > 1 ? ws : nullptr, split_bytes, s, *dev);
+                     L.ksplit > 1 ? ws : nullptr, L.partials_bytes, s, *dev);
 }
 
 int g16_skinny(const void* x, int x_dtype, const uint16_t* w_t, const float* bias, void* out, int out_dtype, int M,

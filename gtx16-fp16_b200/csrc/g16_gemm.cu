@@ -15,15 +15,17 @@
 //     releases smem stages and publishes finished accumulators;
 //   * warps 2-5: epilogue; each reads its 32 TMEM lanes with tcgen05.ld, applies the per-row
 //     power-of-two unscale and fp32 bias, converts and stores, overlapping the next tile's MMAs;
-//   * split-K (few output tiles): each unit writes an fp32 partial tile to the workspace; the last
-//     unit to arrive on a tile (atomic counter, no waiting) sums the partials in split order and
-//     runs the same epilogue, then re-zeroes the counter. Results are bitwise reproducible.
+//   * split-K (few output tiles): each unit writes its fp32 partial tile to the workspace; a
+//     second, fully parallel kernel (launched with programmatic dependent launch so its launch
+//     overlaps the GEMM's tail) sums the partials of every output in split order and applies the
+//     same epilogue. No atomics and no waiting: results are bitwise reproducible.
 // Every wait is bounded; on expiry the kernel records G16_ERR_TIMEOUT in the device status word,
 // drains its in-flight copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "g16_internal.cuh"
@@ -47,8 +49,7 @@ struct GemmArgs {
   void* out;
   const float* bias;
   const float* rscale;
-  float* partials;  // [tiles][ksplit][kBM][kBN] fp32 (split-K only)
-  int* counters;    // [tiles] (split-K only)
+  float* partials;  // [m_tiles * n_tiles][ksplit][kBM][kBN] fp32 (split-K only), tile = mt * n_tiles + nt
   int* status;      // device status word
   int M, N, K;
   int m_tiles, n_tiles, tiles;
@@ -76,14 +77,10 @@ __device__ __forceinline__ Unit unit_coords(const GemmArgs& a, int u) {
   return r;
 }
 
-__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
 __device__ __forceinline__ void report_timeout(int* status, volatile int* abort_flag) {
   *abort_flag = 1;
   atomicExch(status, G16_ERR_TIMEOUT);
 }
-
-__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 // Store 32 consecutive fp32 results (one row, columns col0..col0+31) with unscale and bias.
 template <bool OUT_F16>
@@ -134,8 +131,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_base_slot + 2);
-  volatile int* stop_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 3);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -275,69 +270,26 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       } else {
-        // All four epilogue warps pass the same three named barriers per unit, even after a
-        // timeout, so none can be left waiting on a hardware barrier; they leave together.
-        if (got) {
-          tc_fence_after();
-          float* my_part = args.partials + (static_cast<size_t>(w.tile) * args.ksplit + w.split) * (kBM * kBN) +
-                           static_cast<size_t>(r_local) * kBN;
+        if (!got) break;
+        tc_fence_after();
+        const int tile_rm = w.mt * args.n_tiles + w.nt;
+        float* my_part = args.partials + (static_cast<size_t>(tile_rm) * args.ksplit + w.split) * (kBM * kBN) +
+                         static_cast<size_t>(r_local) * kBN;
 #pragma unroll 1
-          for (int c = 0; c < kBN / 32; ++c) {
-            uint32_t r[32];
-            __syncwarp();
-            tmem_ld_32x32b_x32(t_row + c * 32, r);
-            tmem_ld_wait();
-            float4* dst = reinterpret_cast<float4*>(my_part + c * 32);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
-          }
-          tc_fence_before();
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-        }
-        // Publish this partial, then count arrivals on the tile; the last arriver reduces.
-        __threadfence();
-        named_sync_epi();
-        if (threadIdx.x == 64) {
-          int last = 0;
-          if (!*abort_flag) {
-            const int prev = atomicAdd(args.counters + w.tile, 1);
-            last = (prev == args.ksplit - 1) ? 1 : 0;
-            if (last) args.counters[w.tile] = 0;  // every split has arrived: reset for the next call
-          }
-          *last_flag = last;
-          __threadfence();
-        }
-        named_sync_epi();
-        if (*last_flag) {
-          __threadfence();
-          const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
-          const float* base = args.partials + static_cast<size_t>(w.tile) * args.ksplit * (kBM * kBN) +
-                              static_cast<size_t>(r_local) * kBN;
-#pragma unroll 1
-          for (int c = 0; c < kBN / 32; ++c) {
-            float v[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+          float4* dst = reinterpret_cast<float4*>(my_part + c * 32);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 t = ldcg4(base + c * 32 + 4 * j);
-              v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
-            }
-            for (int s = 1; s < args.ksplit; ++s) {
-              const float* p = base + static_cast<size_t>(s) * (kBM * kBN) + c * 32;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 t = ldcg4(p + 4 * j);
-                v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
-              }
-            }
-            store_row32<OUT_F16>(args, row, w.nt * kBN + c * 32, rs, v);
-          }
+          for (int j = 0; j < 8; ++j)
+            __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                        __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
         }
-        if (threadIdx.x == 64) *stop_flag = *abort_flag;
-        named_sync_epi();  // last_flag / stop_flag are reused by the next unit
-        if (*stop_flag) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
@@ -352,39 +304,59 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   }
 }
 
+// Split-K reduction: out = (sum over splits s = 0..ksplit-1, in order, of partial[tile][s]) * rscale
+// + bias. One thread per 4 consecutive output columns of one row; launched with programmatic
+// dependent launch, so it waits here for the GEMM grid's partial stores.
+template <bool OUT_F16>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs args) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  constexpr int kQuads = kBN / 4;
+  const size_t total = static_cast<size_t>(args.m_tiles) * args.n_tiles * kBM * kQuads;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int q = static_cast<int>(i % kQuads);
+    const size_t t1 = i / kQuads;
+    const int r = static_cast<int>(t1 % kBM);
+    const size_t tile = t1 / kBM;
+    const int mt = static_cast<int>(tile / args.n_tiles);
+    const int nt = static_cast<int>(tile % args.n_tiles);
+    const int row = mt * kBM + r;
+    const int col = nt * kBN + 4 * q;
+    if (row >= args.M || col >= args.N) continue;
+    const float* p = args.partials + tile * args.ksplit * static_cast<size_t>(kBM * kBN) + r * kBN + 4 * q;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(p));
+    int s = 1;
+    for (; s + 3 < args.ksplit; s += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(p + static_cast<size_t>(s + u) * (kBM * kBN)));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) { acc.x += v[u].x; acc.y += v[u].y; acc.z += v[u].z; acc.w += v[u].w; }
+    }
+    for (; s < args.ksplit; ++s) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(p + static_cast<size_t>(s) * (kBM * kBN)));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    const float rs = args.rscale != nullptr ? __ldg(args.rscale + row) : 1.f;
+    float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (args.bias != nullptr) b = __ldg(reinterpret_cast<const float4*>(args.bias + col));
+    const float o0 = fmaf(acc.x, rs, b.x), o1 = fmaf(acc.y, rs, b.y), o2 = fmaf(acc.z, rs, b.z), o3 = fmaf(acc.w, rs, b.w);
+    const size_t off = static_cast<size_t>(row) * args.N + col;
+    if constexpr (OUT_F16) {
+      const __half2 h0 = __floats2half2_rn(o0, o1), h1 = __floats2half2_rn(o2, o3);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t*>(&h0);
+      u.y = *reinterpret_cast<const uint32_t*>(&h1);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(args.out) + off) = u;
+    } else {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + off) = make_float4(o0, o1, o2, o3);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn(int* status) {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  if (fn == nullptr) *status = err != cudaSuccess ? cuda_fail(err) : G16_ERR_CUDA;
-  return fn;
-}
-
-// 2-D fp16 tensor map over a row-major [rows, cols] matrix with a [box_rows, 64] box and 128-byte
-// swizzle (64 fp16 = 128 bytes per box row).
-int make_tmap_fp16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
-  int st = G16_OK;
-  auto fn = encode_fn(&st);
-  if (fn == nullptr) return st;
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {64, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? G16_OK : G16_ERR_CUDA;
-}
-
 size_t partial_bytes(int tiles, int ksplit) {
   return static_cast<size_t>(tiles) * ksplit * kBM * kBN * sizeof(float);
 }
@@ -400,15 +372,53 @@ int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev) {
   int ks = dev.sm_count / tiles;
   const int by_k = kblocks / 4;  // keep at least 4 k-blocks (256 of K) per split
   if (ks > by_k) ks = by_k;
-  if (tiles * 4 > static_cast<int>(kCounterBytes)) return 1;
   return ks < 1 ? 1 : ks;
 }
 
 size_t gemm_workspace_bytes(int M, int K, int N, int ksplit) {
   if (ksplit <= 1) return 0;
-  (void)K;
-  return kCounterBytes + partial_bytes(tiles_of(M, N), ksplit);
+  const int kblocks = (K + kBK - 1) / kBK;
+  if (ksplit > kblocks) ksplit = kblocks;
+  return partial_bytes(tiles_of(M, N), ksplit);
 }
+
+namespace {
+
+// cudaFuncSetAttribute once per (kernel, device): the call costs microseconds on the host.
+template <typename F>
+cudaError_t ensure_smem_attr(F* kern, std::atomic<uint64_t>& done, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+std::atomic<uint64_t> g_attr_f16{0}, g_attr_f32{0};
+
+template <bool OUT_F16>
+cudaError_t launch_reduce(const GemmArgs& args, cudaStream_t s, const DeviceInfo& dev) {
+  const size_t total = static_cast<size_t>(args.m_tiles) * args.n_tiles * kBM * (kBN / 4);
+  size_t blocks = (total + 255) / 256;
+  const size_t cap = static_cast<size_t>(dev.sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<OUT_F16>, args);
+}
+
+}  // namespace
 
 int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                 const float* rscale, int M, int K, int N, int ksplit, void* ws, size_t ws_bytes, cudaStream_t s,
@@ -435,34 +445,40 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
   args.ksplit = ksplit;
   args.units = args.tiles * ksplit;
   if (ksplit > 1) {
-    if (args.tiles * 4 > static_cast<int>(kCounterBytes)) return G16_ERR_ARG;
-    const size_t need = kCounterBytes + partial_bytes(args.tiles, ksplit);
+    const size_t need = partial_bytes(args.tiles, ksplit);
     if (ws == nullptr || ws_bytes < need) return G16_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return G16_ERR_ALIGN;
-    args.counters = static_cast<int*>(ws);
-    args.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
+    args.partials = static_cast<float*>(ws);
   }
 
   CUtensorMap ta, tb;
-  int st = make_tmap_fp16(&ta, a16, static_cast<uint64_t>(M), static_cast<uint64_t>(K), kBM);
+  // A: [M, K] K-major, [128 x 64] boxes; B: [K, N] N-major, [64 x 64] boxes; 128-byte swizzle.
+  int st = make_tmap_2d(&ta, a16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(M),
+                        static_cast<uint64_t>(K), kBM, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
-  st = make_tmap_fp16(&tb, b16, static_cast<uint64_t>(K), static_cast<uint64_t>(N), kBK);
+  st = make_tmap_2d(&tb, b16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                    kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
 
   const int grid = args.units < dev.sm_count ? args.units : dev.sm_count;
   cudaError_t e;
   if (out_dtype == G16_F16) {
-    e = cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    e = ensure_smem_attr(gemm_kernel<true>, g_attr_f16, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return cuda_fail(e);
     gemm_kernel<true><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
   } else {
-    e = cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    e = ensure_smem_attr(gemm_kernel<false>, g_attr_f32, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return cuda_fail(e);
     gemm_kernel<false><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();
+  if (ksplit > 1) {
+    e = out_dtype == G16_F16 ? launch_reduce<true>(args, s, dev) : launch_reduce<false>(args, s, dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    note_launch();
+  }
   return G16_OK;
 }
 

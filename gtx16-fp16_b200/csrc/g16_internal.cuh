@@ -1,6 +1,7 @@
 // Internal declarations shared by the kernel translation units and the C-ABI layer.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -41,6 +42,10 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
 size_t gemm_workspace_bytes(int M, int K, int N, int ksplit);
 int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
 
+// 2-D TMA tensor map over a row-major [rows, cols] matrix with a [box_rows, box_cols] box (g16_tmap.cu).
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes, uint64_t rows,
+                 uint64_t cols, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swz);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // GEMM tile geometry (also used for workspace sizing on the host).
@@ -48,8 +53,5 @@ constexpr int kBM = 128;   // UMMA M (one CTA, cta_group::1)
 constexpr int kBN = 256;   // UMMA N
 constexpr int kBK = 64;    // K per pipeline stage: one 128-byte swizzle row of fp16
 constexpr int kUmmaK = 16; // K per tcgen05.mma for 16-bit inputs
-
-// Split-K workspace layout: [kCounterBytes of per-tile arrival counters][partials fp32].
-constexpr size_t kCounterBytes = 4096;
 
 }  // namespace g16

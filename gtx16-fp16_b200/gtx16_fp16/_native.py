@@ -93,16 +93,16 @@ def stream_handle(device_index: int) -> int:
 
 
 # ---------------------------------------------------------------------------------------------
-# Workspace: one zero-initialised buffer per (device, stream), grown on demand. Its first 4 KiB hold
-# split-K arrival counters that every completed call leaves at zero, so the buffer is reused
-# without re-zeroing. Calls on the same stream are ordered, so sharing it across calls is safe.
+# Workspace: one buffer per (device, stream), grown on demand. It holds split-K partial tiles and the
+# fp16 copy of fp32 activations; no initial contents are needed. Calls on the same stream are
+# ordered, so sharing it across calls is safe.
 # ---------------------------------------------------------------------------------------------
 _ws: dict[tuple[int, int], torch.Tensor] = {}
 _ws_lock = threading.Lock()
 
 
 def workspace(device: torch.device, stream: int, nbytes: int) -> tuple[int, int]:
-    """(pointer, size) of a zeroed workspace of at least nbytes for this device and stream."""
+    """(pointer, size) of a workspace of at least nbytes for this device and stream."""
     if nbytes <= 0:
         return 0, 0
     key = (device.index or 0, stream)
@@ -112,7 +112,7 @@ def workspace(device: torch.device, stream: int, nbytes: int) -> tuple[int, int]
             buf = _ws.get(key)
             if buf is None or buf.numel() < nbytes:
                 size = max(nbytes, 0 if buf is None else 2 * buf.numel())
-                buf = torch.zeros(size, dtype=torch.uint8, device=device)
+                buf = torch.empty(size, dtype=torch.uint8, device=device)
                 _ws[key] = buf
     return buf.data_ptr(), buf.numel()
 

@@ -55,9 +55,9 @@ enum g16_status {
  *   w_t      [K,N] row-major fp16, 16-byte aligned
  *   bias     [N] fp32 or NULL
  *   out      [M,N] row-major, dtype out_dtype, 16-byte aligned, must not alias any input
- *   workspace/workspace_bytes: scratch of at least g16_mm_t_workspace_bytes(M,K,N,x_dtype);
- *            its first 4 KiB must be zero before the first call and are left zero by every call
- *            that completes; may be NULL when that size is 0.
+ *   workspace/workspace_bytes: scratch of at least g16_mm_t_workspace_bytes(M,K,N,x_dtype) bytes,
+ *            256-byte aligned, no initial contents required; may be NULL when that size is 0.
+ *            Calls that may overlap on the GPU (different streams) need separate workspaces.
  * Requires K % 8 == 0, N % 8 == 0, M >= 0 (M == 0 is a no-op).
  */
 int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, void* out, int out_dtype, int M, int K,
