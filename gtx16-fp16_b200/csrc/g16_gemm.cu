@@ -131,6 +131,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+  // Self-check: the layout must end inside the launch's dynamic shared memory (uniform for the
+  // whole grid: every CTA returns before any barrier, TMEM allocation or shared-memory access).
+  if (static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) > dynamic_smem_bytes()) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(args.status, G16_ERR_ARG);
+    return;
+  }
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;

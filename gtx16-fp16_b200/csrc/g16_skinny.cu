@@ -101,6 +101,13 @@ skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args)
   uint64_t* empty_bar = full_bar + kStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + kStages);
   float* red = reinterpret_cast<float*>(ring);  // [kRowLanes][M][kStrip], after the main loop
+  // Self-check: the layout must end inside the launch's dynamic shared memory (uniform for the
+  // whole grid, so every CTA returns before any barrier or shared-memory access).
+  const uint32_t layout_end = static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw);
+  if (layout_end > dynamic_smem_bytes()) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicExch(args.status, G16_ERR_ARG);
+    return;
+  }
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -247,6 +254,12 @@ struct SkinnyPlan {
   size_t smem_bytes;
 };
 
+size_t skinny_smem_bytes(int M, int piece) {
+  const int mp = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
+  return 1024 + static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(piece) * mp * 4 +
+         static_cast<size_t>(M) * kStrip * 4 + 2 * kStages * 8 + 16;
+}
+
 SkinnyPlan plan_skinny(int M, int K, int N, int sm_count) {
   SkinnyPlan p{};
   p.strips = (N + kStrip - 1) / kStrip;
@@ -265,9 +278,7 @@ SkinnyPlan plan_skinny(int M, int K, int N, int sm_count) {
   p.csize = c;
   p.kchunk = kchunk;
   p.piece = kchunk < kPieceMax ? kchunk : kPieceMax;
-  const int mp = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
-  p.smem_bytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(p.piece) * mp * 4 +
-                 static_cast<size_t>(M) * kStrip * 4 + 2 * kStages * 8 + 16;
+  p.smem_bytes = skinny_smem_bytes(M, p.piece);
   return p;
 }
 
@@ -311,7 +322,9 @@ int plan_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan* ou
   int devid = 0;
   cudaError_t e = cudaGetDevice(&devid);
   if (e != cudaSuccess) return cuda_fail(e);
-  const uint64_t key = (static_cast<uint64_t>(devid) << 56) ^ (static_cast<uint64_t>(K) << 28) ^ static_cast<uint64_t>(N);
+  // Every instantiation shares this cache (same kernel function type), and the layout depends on M.
+  const uint64_t key = (static_cast<uint64_t>(devid) << 58) ^ (static_cast<uint64_t>(M) << 54) ^
+                       (static_cast<uint64_t>(K) << 27) ^ static_cast<uint64_t>(N);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -349,6 +362,8 @@ int launch_skinny_t(const void* x, const uint16_t* w, const float* bias, void* o
   SkinnyPlan p;
   int st0 = plan_for(kern, M, K, N, dev, &p);
   if (st0 != G16_OK) return st0;
+  if (p.smem_bytes < skinny_smem_bytes(M, p.piece) || p.smem_bytes > static_cast<size_t>(kSmemAttrBytes))
+    return G16_ERR_ARG;
   CUtensorMap tmap;
   int st = make_tmap_2d(&tmap, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                         kBoxRows, kStrip, CU_TENSOR_MAP_SWIZZLE_NONE);
