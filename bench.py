@@ -297,13 +297,14 @@ def timed_loop(wl, g16, steps, stream, graph=None):
     With `graph` (a CUDA graph holding exactly `steps` captured steps) the steps are replayed from
     the graph, so host launch overhead does not stretch microsecond-scale steps."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    if graph is not None:
-        graph.replay()
-    else:
-        for _ in range(steps):
-            wl.step(g16)
-    end.record(stream)
+    with torch.cuda.stream(stream):  # replay() and the steps launch on the current stream
+        start.record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(steps):
+                wl.step(g16)
+        end.record(stream)
     end.synchronize()
     return start.elapsed_time(end)
 
@@ -341,7 +342,8 @@ def run_ours(args, rank, world, dev):
         gstream = torch.cuda.Stream(dev)
         graph, launches = capture_steps(wl, g16, args.steps, gstream)
         stream = gstream
-        graph.replay()  # one untimed replay: the warm-up of the captured work
+        with torch.cuda.stream(stream):
+            graph.replay()  # one untimed replay: the warm-up of the captured work
         torch.cuda.synchronize(dev)
 
     sampler = ClockSampler(dev.index or 0)
@@ -425,7 +427,8 @@ def sub_metrics(args, dev, g16, peaks):
         if args.graph:
             stream = torch.cuda.Stream(dev)
             graph, _ = capture_steps(wl, g16, steps, stream)
-            graph.replay()
+            with torch.cuda.stream(stream):
+                graph.replay()
             torch.cuda.synchronize(dev)
         ms = timed_loop(wl, g16, steps, stream, graph) / steps
         if wl.unit == "TFLOPS":
