@@ -139,6 +139,8 @@ class Workload:
     metric = ""
     unit = ""
     bound = "tensor"
+    graphable = True
+    scaling = "weak"
 
     def __init__(self, dev):
         self.dev = dev
@@ -277,16 +279,181 @@ class MmT(Workload):
             f"fp32 F.linear {rows}x{self.K}x{self.N} (reference linear.py fallback)"
 
 
+class ShardedGemm(Workload):
+    """16384^3 fp16 GEMM with w_t split by columns over the ranks (1/2/4/8 GPUs):
+    each rank holds A (replicated) and its column shard of B, computes its output columns with
+    gtx16_fp16.mm_t and the shards are exchanged with one NCCL all-gather (gtx16_fp16.dist).
+    A step ends with the full C on every rank. Total work is fixed: strong scaling."""
+    bound = "tensor"
+    graphable = False
+
+    def __init__(self, dev, world, rank, M=16384, K=16384, N=16384):
+        super().__init__(dev)
+        from gtx16_fp16.dist import ShardedMatmul, shard_bounds
+        self.M, self.K, self.N, self.world, self.rank = M, K, N, world, rank
+        self.name = "gemm16384"
+        self.metric = f"GEMM TFLOPS (fp16 {M}x{K}x{N}, N-sharded over GPUs + NCCL all-gather)"
+        self.unit = "TFLOPS"
+        self.scaling = "strong"
+        g = torch.Generator(device=dev).manual_seed(0)
+        self.A = torch.randn(M, K, device=dev, generator=g).half()
+        n0, n1 = shard_bounds(N, world, rank)
+        b = torch.empty(K, n1 - n0, device=dev, dtype=torch.float16)
+        # B ~ N(0, 1/sqrt(K)) generated in 2048-column panels so every rank draws the same B
+        for c0 in range(0, N, 2048):
+            panel = (torch.randn(K, min(2048, N - c0), device=dev, generator=g) * K ** -0.5).half()
+            lo, hi = max(c0, n0), min(c0 + panel.shape[1], n1)
+            if lo < hi:
+                b[:, lo - n0:hi - n0] = panel[:, lo - c0:hi - c0]
+            del panel
+        self.B = b
+        self.sm = ShardedMatmul(self.B, N, out_dtype=torch.float16)
+
+    def config(self):
+        return {"workload": self.name, "M": self.M, "K": self.K, "N": self.N, "in": "fp16", "out": "fp16",
+                "shard": f"w_t columns [{self.sm.n0}, {self.sm.n1}) on rank {self.rank}",
+                "inputs": "A~N(0,1), B~N(0,1/sqrt(K)) fp16, seed 0 (BASELINE config 3)",
+                "l2": "A alone is 512 MiB > 126 MB L2"}
+
+    def flops(self):
+        return 2.0 * self.M * self.N * self.K / self.world  # per rank (value sums over ranks)
+
+    def alg_bytes(self):
+        return 2.0 * (self.M * self.K + self.K * self.N / self.world + self.M * self.N)
+
+    def step(self, g16):
+        return self.sm(self.A)
+
+    def local_step(self, g16):
+        return self.sm.local(self.A)
+
+    def host_inputs(self):
+        return [self.A.cpu().pin_memory(), self.B.cpu().pin_memory()]
+
+    def host_out(self):
+        return torch.empty(self.M, self.N, dtype=torch.float16).pin_memory()
+
+    def e2e_step(self, g16, hin, hout):
+        a = hin[0].to(self.dev, non_blocking=True)
+        self.B.copy_(hin[1], non_blocking=True)
+        hout.copy_(self.sm(a), non_blocking=True)
+
+    def cpu_sample(self):
+        rows = 256
+        a = self.A[:rows].float().cpu()
+        b = self.B[:, : min(2048, self.B.shape[1])].float().cpu()
+        return (lambda: torch.matmul(a, b)), 2.0 * rows * b.shape[1] * self.K, \
+            f"fp32 torch.matmul {rows}x{self.K}x{b.shape[1]} (a block of the workload)"
+
+
+class Bert(Workload):
+    """BERT-base encoder inference with every Linear patched to FastLinear:
+    random init (seed 0), fp32 activations, 256 sequences x 256 tokens, ids uniform in
+    [1000, 30521], full attention mask. Data parallel: rank r runs its slice of the 256 sequences;
+    value = 256 / (max-rank step time). The CLS embeddings are L2-normalised and compared with the
+    unpatched fp32 model (cosine >= 0.9999)."""
+    bound = "tensor"
+    graphable = False
+
+    def __init__(self, dev, world, rank, batch=256, seq=256, reference=False):
+        super().__init__(dev)
+        import copy
+        import gtx16_fp16 as g16
+        from gtx16_fp16.dist import batch_slice
+        from transformers import BertConfig, BertModel
+        self.name = "bert"
+        self.metric = "BERT-base texts/s (256 x 256 tokens, FastLinear, data parallel)"
+        self.unit = "texts/s"
+        self.scaling = "strong"
+        self.world, self.rank, self.batch, self.seq = world, rank, batch, seq
+        cfg = BertConfig(vocab_size=30522, hidden_size=768, num_hidden_layers=12, num_attention_heads=12,
+                         intermediate_size=3072, hidden_act="gelu", max_position_embeddings=512,
+                         attn_implementation="sdpa")
+        self.cfg = cfg
+        self.n_patched = 0
+        if not reference:  # the reference arm only runs the CPU model (cpu_sample)
+            torch.manual_seed(0)
+            model = BertModel(cfg).eval()
+            self.ref_model = copy.deepcopy(model).to(dev)
+            self.model = model.to(dev)
+            self.n_patched = g16.patch(self.model, force=True)
+        gen = torch.Generator().manual_seed(0)
+        ids = torch.randint(1000, 30522, (batch, seq), generator=gen)
+        sl = batch_slice(batch, world, rank)
+        self.local_batch = sl.stop - sl.start
+        self.ids_host = ids[sl].contiguous()
+        self.ids = self.ids_host.to(dev) if not reference else None
+        self.mask = torch.ones_like(self.ids) if not reference else None
+        self.cos_min = None
+
+    def config(self):
+        return {"workload": self.name, "model": "BERT-base (12 x 768, 12 heads, FFN 3072, random init seed 0)",
+                "global_batch": self.batch, "seq_len": self.seq, "local_batch": self.local_batch,
+                "patched_linears": self.n_patched, "activations": "fp32", "attention": "torch sdpa (fp32)",
+                "cosine_min_vs_fp32": self.cos_min, "l2": "activations 200+ MB per layer > 126 MB L2"}
+
+    def flops(self):  # Linear FLOPs of this rank's slice (the part that runs on libg16)
+        tokens = self.local_batch * self.seq
+        return 2.0 * tokens * 12 * (4 * 768 * 768 + 2 * 768 * 3072) + 2.0 * self.local_batch * 768 * 768
+
+    def alg_bytes(self):
+        return 0.0
+
+    def step(self, g16):
+        with torch.no_grad():
+            return self.model(input_ids=self.ids, attention_mask=self.mask).last_hidden_state[:, 0]
+
+    def check_cosine(self):
+        with torch.no_grad():
+            ref = self.ref_model(input_ids=self.ids, attention_mask=self.mask).last_hidden_state[:, 0]
+            got = self.step(None)
+        ref = torch.nn.functional.normalize(ref.float(), dim=-1)
+        got = torch.nn.functional.normalize(got.float(), dim=-1)
+        self.cos_min = round(float((ref * got).sum(-1).min()), 7)
+        del self.ref_model
+        torch.cuda.empty_cache()
+        return self.cos_min
+
+    def host_inputs(self):
+        return [self.ids_host.pin_memory()]
+
+    def host_out(self):
+        return torch.empty(self.local_batch, 768, dtype=torch.float32).pin_memory()
+
+    def e2e_step(self, g16, hin, hout):
+        ids = hin[0].to(self.dev, non_blocking=True)
+        with torch.no_grad():
+            cls = self.model(input_ids=ids, attention_mask=torch.ones_like(ids)).last_hidden_state[:, 0]
+        hout.copy_(torch.nn.functional.normalize(cls, dim=-1), non_blocking=True)
+
+    def cpu_sample(self):
+        """The reference CPU path for this model: the unpatched fp32 model on the host (4 sequences)."""
+        import copy
+        from transformers import BertConfig, BertModel
+        torch.manual_seed(0)
+        cpu_model = BertModel(self.cfg).eval()
+        ids = self.ids_host[:4]
+        mask = torch.ones_like(ids)
+
+        def run():
+            with torch.no_grad():
+                cpu_model(input_ids=ids, attention_mask=mask)
+        return run, 4.0, "unpatched fp32 BERT-base forward, 4 x 256 tokens on the host"
+
+
 WORKLOADS = {
-    "gemm4096": lambda dev: Gemm(dev, 4096, 4096, 4096, "gemm4096"),
-    "splitk": lambda dev: Gemm(dev, 128, 16384, 1024, "splitk"),
-    "splitk64": lambda dev: Gemm(dev, 64, 1024, 1024, "splitk64"),
-    "gemm16384": lambda dev: Gemm(dev, 16384, 16384, 16384, "gemm16384"),
-    "skinny": lambda dev: MmT(dev, 8, 4096, 4096, "skinny", torch.float32, torch.float32, 0.02, 0.01),
-    "skinny1": lambda dev: MmT(dev, 1, 4096, 4096, "skinny1", torch.float32, torch.float32, 0.02, 0.01),
-    "skinny4": lambda dev: MmT(dev, 4, 4096, 4096, "skinny4", torch.float32, torch.float32, 0.02, 0.01),
-    "rescale": lambda dev: MmT(dev, 2048, 3072, 1024, "rescale", torch.float32, torch.float32, 0.02, 0.0,
-                               rescale=True),
+    "gemm4096": lambda dev, w, r: Gemm(dev, 4096, 4096, 4096, "gemm4096"),
+    "gemm1024": lambda dev, w, r: Gemm(dev, 1024, 1024, 1024, "gemm1024"),
+    "splitk": lambda dev, w, r: Gemm(dev, 128, 16384, 1024, "splitk"),
+    "splitk64": lambda dev, w, r: Gemm(dev, 64, 1024, 1024, "splitk64"),
+    "gemm16384": lambda dev, w, r: ShardedGemm(dev, w, r),
+    "skinny": lambda dev, w, r: MmT(dev, 8, 4096, 4096, "skinny", torch.float32, torch.float32, 0.02, 0.01),
+    "skinny1": lambda dev, w, r: MmT(dev, 1, 4096, 4096, "skinny1", torch.float32, torch.float32, 0.02, 0.01),
+    "skinny4": lambda dev, w, r: MmT(dev, 4, 4096, 4096, "skinny4", torch.float32, torch.float32, 0.02, 0.01),
+    "skinny1x3072": lambda dev, w, r: MmT(dev, 1, 1024, 3072, "skinny1x3072", torch.float32, torch.float32, 0.02, 0.01),
+    "rescale": lambda dev, w, r: MmT(dev, 2048, 3072, 1024, "rescale", torch.float32, torch.float32, 0.02, 0.0,
+                                     rescale=True),
+    "bert": lambda dev, w, r: Bert(dev, w, r),
 }
 
 
@@ -332,13 +499,15 @@ def run_ours(args, rank, world, dev):
     from gtx16_fp16 import _native
 
     peaks, peak_src = load_peaks()
-    wl = WORKLOADS[args.workload](dev)
+    wl = WORKLOADS[args.workload](dev, world, rank)
+    if isinstance(wl, Bert):
+        wl.check_cosine()
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         wl.step(g16)
     torch.cuda.synchronize(dev)
     graph = None
-    if args.graph:
+    if args.graph and wl.graphable:
         gstream = torch.cuda.Stream(dev)
         graph, launches = capture_steps(wl, g16, args.steps, gstream)
         stream = gstream
@@ -360,8 +529,15 @@ def run_ours(args, rank, world, dev):
     ms_max = reduce_max(ms, world, dev)
     ms_step = ms_max / args.steps
 
-    per_rank_units = wl.flops() / 1e12 if wl.unit == "TFLOPS" else wl.alg_bytes() / 1e9
+    if wl.unit == "TFLOPS":
+        per_rank_units = wl.flops() / 1e12
+    elif wl.unit == "texts/s":
+        per_rank_units = float(wl.local_batch)
+    else:
+        per_rank_units = wl.alg_bytes() / 1e9
     value = world * per_rank_units / (ms_step * 1e-3)
+    if wl.unit == "texts/s":
+        value = wl.batch / (ms_step * 1e-3)  # the whole batch per max-rank step time
 
     # e2e through the public API with host buffers
     stream = torch.cuda.current_stream(dev)
@@ -394,15 +570,19 @@ def run_ours(args, rank, world, dev):
     roof = {"bound": wl.bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "traffic": traffic,
             "peak_source": f"{peak_src} ({'bf16_tflops burst' if wl.bound == 'tensor' else 'hbm_gbs copy'})",
-            "basis": (f"2*M*N*K = {wl.flops():.4g} FLOP per launch" if wl.bound == "tensor" else
+            "basis": (f"Linear FLOPs of the rank's slice = {wl.flops():.4g} per step (rate over the whole step)"
+                      if wl.unit == "texts/s" else
+                      f"2*M*N*K = {wl.flops():.4g} FLOP per launch" if wl.bound == "tensor" else
                       f"2KN+xMK+4N+oMN = {wl.alg_bytes():.4g} B per launch"),
             "launches_per_step": launches / max(args.steps, 1)}
 
     line = {"metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
-            "config": dict(wl.config(), parallelism=f"replicas x{world}"),
-            "e2e": {"value": round(world * per_rank_units / (e2e_ms * 1e-3), 3), "unit": wl.unit,
+            "scaling": wl.scaling, "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
+            "config": dict(wl.config(), parallelism=(f"replicas x{world}" if wl.scaling == "weak" else
+                                                     (f"dp{world}" if wl.unit == "texts/s" else f"n-shard{world}"))),
+            "e2e": {"value": round((wl.batch if wl.unit == "texts/s" else world * per_rank_units) / (e2e_ms * 1e-3), 3),
+                    "unit": wl.unit,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms, 4), "api": "gtx16_fp16 public API, pinned host buffers"},
             "roofline": roof, "gpu_launches": int(launches), "clocks": sampler.summary(), "impl": "ours",
@@ -418,20 +598,23 @@ def sub_metrics(args, dev, g16, peaks):
     """Short measurements of the other BASELINE configs (same timing rules), for context."""
     out = {}
     for name in [n for n in args.extra.split(",") if n and n != args.workload]:
-        wl = WORKLOADS[name](dev)
+        wl = WORKLOADS[name](dev, 1, 0)
         for _ in range(5):
             wl.step(g16)
         torch.cuda.synchronize(dev)
         steps = 50 if name != "gemm16384" else 10
         graph, stream = None, torch.cuda.current_stream(dev)
-        if args.graph:
+        if args.graph and wl.graphable:
             stream = torch.cuda.Stream(dev)
             graph, _ = capture_steps(wl, g16, steps, stream)
             with torch.cuda.stream(stream):
                 graph.replay()
             torch.cuda.synchronize(dev)
         ms = timed_loop(wl, g16, steps, stream, graph) / steps
-        if wl.unit == "TFLOPS":
+        if wl.unit == "texts/s":
+            v = wl.batch / (ms * 1e-3)
+            frac = wl.flops() / (ms * 1e-3) / 1e12 / peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        elif wl.unit == "TFLOPS":
             v = wl.flops() / (ms * 1e-3) / 1e12
             frac = v / peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
         else:
@@ -457,12 +640,17 @@ def cpu_baseline(wl):
         if time.perf_counter() - t0 > 3.0 or n >= 20:
             break
     dt = (time.perf_counter() - t0) / n
+    return {"value": round(cpu_value(wl, units, dt), 5), "unit": wl.unit, "cores": cores, "kind": "port",
+            "sample": sample, "seconds_per_sample": round(dt, 4)}
+
+
+def cpu_value(wl, units, dt):
+    """Convert a CPU sample (units of work in dt seconds) to the workload's metric unit."""
     if wl.unit == "TFLOPS":
-        v = units / dt / 1e12
-    else:  # GB/s of the same algorithmic bytes, scaled to the sample
-        v = wl.alg_bytes() * (units / wl.flops()) / dt / 1e9
-    return {"value": round(v, 5), "unit": wl.unit, "cores": cores, "kind": "port", "sample": sample,
-            "seconds_per_sample": round(dt, 4)}
+        return units / dt / 1e12
+    if wl.unit == "texts/s":
+        return units / dt
+    return wl.alg_bytes() * (units / wl.flops()) / dt / 1e9  # GB/s of the same algorithmic bytes
 
 
 def run_reference(args, rank, world, dev):
@@ -470,7 +658,7 @@ def run_reference(args, rank, world, dev):
     if rank != 0:
         return None
     from oracle import cpu_path
-    wl = WORKLOADS[args.workload](dev)
+    wl = Bert(dev, 1, 0, reference=True) if args.workload == "bert" else WORKLOADS[args.workload](dev, 1, 0)
     cores = cpu_path.use_all_cores()
     fn, units, sample = wl.cpu_sample()
     for _ in range(args.warmup):
@@ -479,9 +667,9 @@ def run_reference(args, rank, world, dev):
     for _ in range(args.steps):
         fn()
     dt = (time.perf_counter() - t0) / args.steps
-    v = units / dt / 1e12 if wl.unit == "TFLOPS" else wl.alg_bytes() * (units / wl.flops()) / dt / 1e9
+    v = cpu_value(wl, units, dt)
     return {"metric": wl.metric, "value": round(v, 5), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": wl.scaling,
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "config": dict(wl.config(), parallelism="cpu"),
             "impl": "reference",
             "cpu_baseline": {"value": round(v, 5), "unit": wl.unit, "cores": cores, "kind": "port", "sample": sample},

@@ -1,0 +1,44 @@
+"""Model-level GPU checks: BERT-base patched with FastLinear against the unpatched fp32 model
+(BASELINE config 5 at a reduced batch), and the column-sharded matmul on one GPU."""
+import copy
+
+import pytest
+import torch
+
+import gtx16_fp16 as g
+from gtx16_fp16.dist import ShardedMatmul, shard_bounds
+
+pytestmark = pytest.mark.gpu
+
+
+def test_bert_base_patched_cosine(cuda_ok):
+    transformers = pytest.importorskip("transformers")
+    cfg = transformers.BertConfig(vocab_size=30522, hidden_size=768, num_hidden_layers=12, num_attention_heads=12,
+                                  intermediate_size=3072, hidden_act="gelu", max_position_embeddings=512,
+                                  attn_implementation="sdpa")
+    torch.manual_seed(0)
+    model = transformers.BertModel(cfg).eval()
+    ref_model = copy.deepcopy(model).cuda()
+    model = model.cuda()
+    assert g.patch(model, force=True) == 73  # 12 x (q, k, v, attn-out, intermediate, output) + pooler
+    gen = torch.Generator().manual_seed(0)
+    ids = torch.randint(1000, 30522, (16, 256), generator=gen).cuda()
+    mask = torch.ones_like(ids)
+    with torch.no_grad():
+        ref = ref_model(input_ids=ids, attention_mask=mask).last_hidden_state[:, 0]
+        got = model(input_ids=ids, attention_mask=mask).last_hidden_state[:, 0]
+    ref = torch.nn.functional.normalize(ref.float(), dim=-1)
+    got = torch.nn.functional.normalize(got.float(), dim=-1)
+    cos = (ref * got).sum(-1)
+    assert cos.min().item() >= 0.9999, cos.min().item()
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 1024, 2048), (300, 512, 776)])
+def test_sharded_matmul_single_gpu(cuda_ok, M, K, N):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device="cuda").half()
+    w = (torch.randn(K, N, device="cuda") * K ** -0.5).half()
+    n0, n1 = shard_bounds(N, 1, 0)
+    sm = ShardedMatmul(w[:, n0:n1].contiguous(), N)
+    y = sm(a)
+    assert torch.equal(y, g.mm_t(a, w, None, torch.float16))
