@@ -221,9 +221,11 @@ __device__ __forceinline__ uint32_t map_cluster(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
+// volatile keeps these loads after the (volatile) cluster barrier; without a memory clobber the
+// hardware can still have several in flight when the caller issues them back to back.
 __device__ __forceinline__ float ld_cluster_f32(uint32_t caddr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(caddr) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(caddr));
   return v;
 }
 __device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t caddr) {

@@ -37,6 +37,7 @@ constexpr int kThreads = kConsumers + 32;    // + one producer warp
 constexpr int kRowLanes = kConsumerWarps;    // warp w handles rows w, w+8 of every stage
 constexpr int kPieceMax = 2048;              // rows of x staged in shared memory at a time
 constexpr int kMaxCluster = 16;
+constexpr int kStageBatch = 8;               // x-staging loads in flight per thread
 
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
@@ -93,7 +94,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args) {
   constexpr int MP = MPad<M>::v;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Align by pointer arithmetic on the __shared__ array (an integer round trip would turn
+  // every access into a generic-address load).
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* ring = smem;
   float* xs = reinterpret_cast<float*>(smem + kStages * kStageBytes);
   float* part = xs + args.piece * MP;
@@ -176,9 +179,24 @@ skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args)
     for (int p0 = 0; p0 < nrows; p0 += args.piece) {
       const int plen = min(args.piece, nrows - p0);
       if (p0 > 0) consumer_sync();  // everyone is done with the previous piece of x
-      for (int i = tid; i < plen * MP; i += kConsumers) {
-        const int m = i / plen, k = i - m * plen;
-        xs[k * MP + m] = (m < M) ? to_f32(x[static_cast<size_t>(m) * args.K + kb + p0 + k]) : 0.f;
+      // Stage x[:, piece] transposed to [k][MP] fp32; kStageBatch loads in flight per thread so
+      // the staging costs one memory latency per batch rather than one per element.
+      for (int base = tid; base < plen * MP; base += kConsumers * kStageBatch) {
+        float v[kStageBatch];
+#pragma unroll
+        for (int u = 0; u < kStageBatch; ++u) {
+          const int i = base + u * kConsumers;
+          const int m = i / plen, k = i - m * plen;
+          v[u] = (i < plen * MP && m < M) ? to_f32(x[static_cast<size_t>(m) * args.K + kb + p0 + k]) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kStageBatch; ++u) {
+          const int i = base + u * kConsumers;
+          if (i < plen * MP) {
+            const int m = i / plen, k = i - m * plen;
+            xs[k * MP + m] = v[u];
+          }
+        }
       }
       consumer_sync();
       const int t_end = (p0 + plen + kBoxRows - 1) / kBoxRows;
@@ -235,8 +253,15 @@ skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args)
       const int m = i / kStrip, c = i - m * kStrip;
       const int n = n0 + c;
       if (n < args.N) {
+        // all remote loads in flight first, then the fixed-order sum
+        float pv[kMaxCluster];
+#pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q)
+          pv[q] = q < csize ? ld_cluster_f32(map_cluster(part_addr + 4u * i, q)) : 0.f;
         float s = 0.f;
-        for (int q = 0; q < csize; ++q) s += ld_cluster_f32(map_cluster(part_addr + 4u * i, q));
+#pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q)
+          if (q < csize) s += pv[q];
         if (args.bias != nullptr) s += args.bias[n];
         if constexpr (OUT_F16) {
           reinterpret_cast<__half*>(args.out)[static_cast<size_t>(m) * args.N + n] = __float2half_rn(s);
