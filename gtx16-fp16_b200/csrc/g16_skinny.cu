@@ -37,7 +37,7 @@ constexpr int kThreads = kConsumers + 32;    // + one producer warp
 constexpr int kRowLanes = kConsumerWarps;    // warp w handles rows w, w+8 of every stage
 constexpr int kPieceMax = 2048;              // rows of x staged in shared memory at a time
 constexpr int kMaxCluster = 16;
-constexpr int kStageBatch = 8;               // x-staging loads in flight per thread
+constexpr int kStageBatch = 2;               // x-staging k-batches per thread (x M loads in flight)
 
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
@@ -179,22 +179,24 @@ skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args)
     for (int p0 = 0; p0 < nrows; p0 += args.piece) {
       const int plen = min(args.piece, nrows - p0);
       if (p0 > 0) consumer_sync();  // everyone is done with the previous piece of x
-      // Stage x[:, piece] transposed to [k][MP] fp32; kStageBatch loads in flight per thread so
-      // the staging costs one memory latency per batch rather than one per element.
-      for (int base = tid; base < plen * MP; base += kConsumers * kStageBatch) {
-        float v[kStageBatch];
+      // Stage x[:, piece] transposed to [k][MP] fp32 (rows m >= M are zero). The row index is a
+      // compile-time loop, so there is no per-element division, and each thread keeps
+      // M x kStageBatch loads in flight: one memory latency per batch.
+      for (int k0 = tid; k0 < plen; k0 += kConsumers * kStageBatch) {
+        float v[M][kStageBatch];
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+          for (int u = 0; u < kStageBatch; ++u) {
+            const int k = k0 + u * kConsumers;
+            v[m][u] = k < plen ? to_f32(x[static_cast<size_t>(m) * args.K + kb + p0 + k]) : 0.f;
+          }
 #pragma unroll
         for (int u = 0; u < kStageBatch; ++u) {
-          const int i = base + u * kConsumers;
-          const int m = i / plen, k = i - m * plen;
-          v[u] = (i < plen * MP && m < M) ? to_f32(x[static_cast<size_t>(m) * args.K + kb + p0 + k]) : 0.f;
-        }
+          const int k = k0 + u * kConsumers;
+          if (k < plen) {
 #pragma unroll
-        for (int u = 0; u < kStageBatch; ++u) {
-          const int i = base + u * kConsumers;
-          if (i < plen * MP) {
-            const int m = i / plen, k = i - m * plen;
-            xs[k * MP + m] = v[u];
+            for (int m = 0; m < MP; ++m) xs[k * MP + m] = m < M ? v[m < M ? m : 0][u] : 0.f;
           }
         }
       }
