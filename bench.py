@@ -719,7 +719,7 @@ def main():
     torch.cuda.set_device(dev)
     try:
         if args.impl == "reference":
-            line = run_reference(args, rank, 1, dev)
+            line = run_reference(args, rank, world, dev)
         else:
             line = run_ours(args, rank, world, dev)
         if rank == 0 and line is not None:

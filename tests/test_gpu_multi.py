@@ -1,6 +1,7 @@
 """Column-sharded matmul across 2 GPUs over NCCL (skipped with fewer than 2 GPUs). The gathered
-output equals the single-GPU result bit for bit: every output column is computed by the same
-kernel over the same K order, whichever rank owns it."""
+output equals, bit for bit, the single-GPU results of the same column shards (same kernel, same
+shape, same K order); against the unsharded product it agrees within the GEMM tolerance (a shard
+can get a different automatic K split than the full matrix)."""
 import os
 import socket
 
@@ -35,8 +36,12 @@ def _worker(rank, world, port, ret):
         w = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
         n0, n1 = shard_bounds(N, world, rank)
         y = ShardedMatmul(w[:, n0:n1].contiguous(), N)(a)
+        shards = [g.mm_t(a, w[:, b0:b1].contiguous(), None, torch.float16)
+                  for b0, b1 in (shard_bounds(N, world, r) for r in range(world))]
+        ok = torch.equal(y, torch.cat(shards, dim=1))
+        ref = a.double() @ w.double()
+        ok = ok and ((y.double() - ref).norm() / ref.norm()).item() < 1e-3
         full = g.mm_t(a, w, None, torch.float16)
-        ok = torch.equal(y, full)
         rows = gather_rows(full[batch_slice(M, world, rank)], M)
         ok = ok and torch.equal(rows, full)
         torch.cuda.synchronize()
