@@ -156,6 +156,7 @@ const char* g16_strerror(int status) {
     case G16_ERR_CUDA: return t_last_cuda != 0 ? cudaGetErrorString(static_cast<cudaError_t>(t_last_cuda)) : "CUDA error";
     case G16_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case G16_ERR_TIMEOUT: return "a kernel's bounded device-side wait expired";
+    case G16_ERR_TOO_LARGE: return "split-K partial tiles exceed the fixed 8 MiB scratch array of g16_gemm_static_scratch";
     default: return "unknown g16 status";
   }
 }

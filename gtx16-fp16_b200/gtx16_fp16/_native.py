@@ -18,7 +18,7 @@ G16_F32 = 0
 G16_F16 = 1
 
 OK = 0
-ERR_ARG, ERR_UNSUPPORTED, ERR_ALIGN, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE, ERR_TIMEOUT = range(1, 8)
+ERR_ARG, ERR_UNSUPPORTED, ERR_ALIGN, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE, ERR_TIMEOUT, ERR_TOO_LARGE = range(1, 9)
 
 _lib = None
 _lock = threading.Lock()
@@ -33,6 +33,7 @@ SIGNATURES = {
     "g16_gemm": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "g16_gemm_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g16_gemm_auto_ksplit": (_I, [_I, _I, _I]),
+    "g16_gemm_static_scratch": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P]),
     "g16_device_status": (_I, [ctypes.POINTER(_I), _I, _P]),
     "g16_launch_count": (ctypes.c_uint64, []),
     "g16_strerror": (ctypes.c_char_p, [_I]),

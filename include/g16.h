@@ -37,7 +37,8 @@ enum g16_status {
   G16_ERR_WORKSPACE = 4,   /* workspace missing or smaller than g16_mm_t_workspace_bytes()        */
   G16_ERR_CUDA = 5,        /* a CUDA runtime call failed; see g16_last_cuda_error()               */
   G16_ERR_DEVICE = 6,      /* the current device is not sm_100 (B200-class)                       */
-  G16_ERR_TIMEOUT = 7      /* a kernel's bounded device-side wait expired (pipeline fault)        */
+  G16_ERR_TIMEOUT = 7,     /* a kernel's bounded device-side wait expired (pipeline fault)        */
+  G16_ERR_TOO_LARGE = 8    /* g16_gemm_static_scratch: partials exceed its fixed scratch array    */
 };
 
 /* Largest M served by the skinny (GEMV) path: SKINNY_MAX_M, src/gtx16_fp16/kernels.py:253. */
@@ -97,6 +98,22 @@ size_t g16_gemm_workspace_bytes(int M, int K, int N, int ksplit);
 
 /* The K-split g16_gemm would choose automatically for this shape on the current device. */
 int g16_gemm_auto_ksplit(int M, int K, int N);
+
+/*
+ * No counterpart in the reference: an entry point for callers that cannot allocate device memory
+ * at call time (e.g. servers that reserve all GPU memory for their own pools at start-up, or hosts
+ * that keep cudaMalloc/cudaFree, which can synchronise the device, off latency-critical threads).
+ * Same operation and arguments as g16_gemm without a workspace: split-K partial tiles go to a fixed
+ * array in device memory of G16_STATIC_SCRATCH_BYTES (8 MiB, 64 partial tiles of 128 x 256 fp32),
+ * held by every GPU that loads the library until exit. Problems whose partials do not fit return
+ * G16_ERR_TOO_LARGE; ksplit = 0 picks the usual split, lowered until it fits. Allocates nothing.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture. All calls on a device share the
+ * array: nothing in it needs to start at zero, but calls that overlap on the GPU race on it.
+ */
+#define G16_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
+int g16_gemm_static_scratch(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                            const float* rscale, int M, int K, int N, int ksplit, void* stream);
 
 /* Device-side status word of the current device: G16_OK, or G16_ERR_TIMEOUT if a kernel's
  * bounded wait expired since the last clear. Synchronises `stream`. clear != 0 resets it. */

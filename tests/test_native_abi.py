@@ -43,6 +43,7 @@ def test_status_codes_match_header():
     assert st["G16_ERR_CUDA"] == _native.ERR_CUDA
     assert st["G16_ERR_DEVICE"] == _native.ERR_DEVICE
     assert st["G16_ERR_TIMEOUT"] == _native.ERR_TIMEOUT
+    assert st["G16_ERR_TOO_LARGE"] == _native.ERR_TOO_LARGE
     dt = header_enum("g16_dtype")
     assert dt == {"G16_F32": _native.G16_F32, "G16_F16": _native.G16_F16}
 
@@ -51,7 +52,7 @@ def test_host_only_entry_points():
     from gtx16_fp16 import _native
     L = _native.lib()
     assert L.g16_version() == 100
-    for code in range(0, 8):
+    for code in range(0, 9):
         assert len(L.g16_strerror(code)) > 0
     assert L.g16_strerror(99) == b"unknown g16 status"
     assert L.g16_launch_count() == 0
