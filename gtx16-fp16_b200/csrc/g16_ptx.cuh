@@ -175,7 +175,22 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 16 consecutive fp32 columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (tensor core
+// operand reads, TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 // Shared-memory matrix descriptor (sm_100 format): start address, leading / stride byte offsets
 // (all >> 4), version 1 at bit 46, swizzle mode in bits 61-63 (2 = 128-byte swizzle).
@@ -189,11 +204,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
-// Instruction descriptor for kind::f16: fp16 A and B, fp32 D, A K-major, B K- or MN-major.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool b_mn_major) {
+// Instruction descriptor for kind::f16: fp16 A and B, fp32 D, A and B each K- or MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool b_mn_major, bool a_mn_major = false) {
   return (1u << 4)                              // D format: f32
          | (0u << 7) | (0u << 10)               // A, B format: f16
-         | (0u << 15)                           // A K-major
+         | ((a_mn_major ? 1u : 0u) << 15)       // A major
          | ((b_mn_major ? 1u : 0u) << 16)       // B major
          | (static_cast<uint32_t>(n >> 3) << 17)  // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16

@@ -91,7 +91,7 @@ struct SkinnyArgs {
 // Shared memory: [ring: kStages x 8 KiB | xs: piece x MP fp32 | part: M x kStrip fp32 | barriers].
 template <int M, typename TX, bool OUT_F16>
 __global__ void __launch_bounds__(kThreads, 1)
-skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args) {
+skinny_fma_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args) {
   constexpr int MP = MPad<M>::v;
   extern __shared__ uint8_t smem_raw[];
   // Align by pointer arithmetic on the __shared__ array (an integer round trip would turn
@@ -380,10 +380,10 @@ int plan_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan* ou
 }
 
 template <int M, typename TX, bool OUT_F16>
-int launch_skinny_t(const void* x, const uint16_t* w, const float* bias, void* out, int K, int N, cudaStream_t s,
-                    const DeviceInfo& dev) {
+int launch_skinny_fma_t(const void* x, const uint16_t* w, const float* bias, void* out, int K, int N, cudaStream_t s,
+                        const DeviceInfo& dev) {
   static std::atomic<uint64_t> attr_done{0};
-  auto kern = skinny_kernel<M, TX, OUT_F16>;
+  auto kern = skinny_fma_kernel<M, TX, OUT_F16>;
   cudaError_t e = ensure_attrs(kern, attr_done, kSmemAttrBytes);
   if (e != cudaSuccess) return cuda_fail(e);
   SkinnyPlan p;
@@ -411,6 +411,367 @@ int launch_skinny_t(const void* x, const uint16_t* w, const float* bias, void* o
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();
   return G16_OK;
+}
+
+// =============================================================================================
+// Tensor-core variant (used whenever the CTA's K chunk fits: kchunk <= kTcMaxChunk).
+//
+// The fp32 FMA work of M <= 8 rows (M FMAs per weight element) is moved to the tensor core without
+// losing fp32 accuracy: each CTA scales its chunk of every x row by a power of two s (so the row's
+// |max| lands in [2^14, 2^15)), splits x*s = hi + lo into two fp16 values (hi = fp16(x*s),
+// lo = fp16(x*s - hi); hi + lo carries 22 significant bits, products with fp16 weights are exact,
+// sums are fp32), and computes out^T[n][m'] = sum_k W[k][n] * xhl[m'][k] with
+// tcgen05.mma kind::f16, M=128 (weight columns), N=16 (m' < 8: hi rows, m' >= 8: lo rows), K=16
+// per 16-row stage. W is the MN-major A operand, streamed by TMA in the same 128-byte swizzled
+// layout the GEMM uses for its B operand; xhl is a K-major B operand built in shared memory. The
+// partial for (m, n) is (D[n][m] + D[n][m+8]) / s, then K chunks are reduced across the cluster
+// as in the FMA variant. Work per stage is two MMAs whatever M is.
+// =============================================================================================
+constexpr int kTcBoxCols = 64;                          // one 128-byte swizzle row of fp16
+constexpr int kTcBoxBytes = kBoxRows * kTcBoxCols * 2;  // 2 KiB
+constexpr int kTcThreads = 192;  // warps 0-3: x prep + epilogue, warp 4: TMEM + MMA, warp 5: TMA
+constexpr int kTcXRows = 16;     // UMMA N: x_hi rows 0..7, x_lo rows 8..15
+constexpr int kTcXBlockBytes = kTcXRows * 128;          // one 64-wide K block of xhl (2 KiB)
+constexpr int kTcMaxChunk = 2048;                       // xhl <= 64 KiB of shared memory
+constexpr uint32_t kTcTmemCols = 32;                    // two [128 x 16] fp32 accumulators
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+
+// Power-of-two scale that maps |max| into [2^14, 2^15) (1 for zero rows); writes its reciprocal.
+__device__ __forceinline__ float split_scale(float amax, float* inv) {
+  const int ef = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu);  // biased exponent
+  int e = 141 - ef;                                                       // 15 - unbiased(frexp)
+  e = e < -125 ? -125 : (e > 125 ? 125 : e);
+  *inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+  return __uint_as_float(static_cast<uint32_t>(127 + e) << 23);
+}
+
+template <int M, typename TX, bool OUT_F16>
+__global__ void __launch_bounds__(kTcThreads, 1)
+skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* ring = smem;                                           // kStages x [4 boxes of 16 x 64]
+  const int nkb = (args.kchunk + 63) / 64;                        // 64-wide K blocks of x
+  uint8_t* xhl = ring + kStages * kStageBytes;                    // nkb x 2 KiB, 1 KiB aligned
+  float* part = reinterpret_cast<float*>(xhl + nkb * kTcXBlockBytes);  // [M][kStrip]
+  float* amax_w = part + M * kStrip;                              // [4 warps][8]
+  float* scale_inv = amax_w + 32;                                 // [8]
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(scale_inv + 8);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* xready_bar = empty_bar + kStages;
+  uint64_t* done_bar = xready_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Self-check: the layout must end inside the launch's dynamic shared memory (uniform for the
+  // grid, so every CTA returns before any barrier, TMEM allocation or shared-memory access).
+  if (static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) >
+      dynamic_smem_bytes()) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicExch(args.status, G16_ERR_ARG);
+    return;
+  }
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int rank = blockIdx.x;
+  const int csize = gridDim.x;
+  const int n0 = blockIdx.y * kStrip;
+  const int kb = rank * args.kchunk;
+  const int ke = min(args.K, kb + args.kchunk);
+  const int nrows = max(0, ke - kb);
+  const int nstages = (nrows + kBoxRows - 1) / kBoxRows;
+
+  if (tid == 0) {
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&full_bar[st], 1);
+      mbar_init(&empty_bar[st], 1);
+    }
+    mbar_init(xready_bar, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 5) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_w);
+      uint32_t phase = 0;
+      int stage = 0;
+      bool armed[kStages];
+      uint32_t armed_phase[kStages];
+      for (int st = 0; st < kStages; ++st) { armed[st] = false; armed_phase[st] = 0; }
+      bool ok = true;
+      for (int t = 0; t < nstages; ++t) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+        uint8_t* dst = ring + stage * kStageBytes;
+        mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+        armed[stage] = true;
+        armed_phase[stage] = phase;
+#pragma unroll
+        for (int j = 0; j < kStrip / kTcBoxCols; ++j)
+          tma_load_2d(dst + j * kTcBoxBytes, &tmap_w, &full_bar[stage], n0 + j * kTcBoxCols, kb + t * kBoxRows);
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(args.status, G16_ERR_TIMEOUT);
+        for (int st = 0; st < kStages; ++st)
+          if (armed[st]) mbar_wait(&full_bar[st], armed_phase[st], nullptr);
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      // D[n][m'] += W[k][n] * xhl[m'][k]: A = W (MN-major), B = xhl (K-major), M=128, N=16.
+      constexpr uint32_t idesc = idesc_f16_f32(128, kTcXRows, /*b_mn_major=*/false, /*a_mn_major=*/true);
+      bool ok = mbar_wait(xready_bar, 0, abort_flag);
+      uint32_t phase = 0;
+      int stage = 0;
+      for (int t = 0; t < nstages && ok; ++t) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(ring + stage * kStageBytes);
+        const uint32_t sb = smem_u32(xhl) + (t >> 2) * kTcXBlockBytes + (t & 3) * 32;
+        const uint64_t bdesc = smem_desc_sw128(sb, 16, 1024);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          // columns [128h, 128h + 128): two 64-column boxes, 2 KiB apart (LBO); 8-row k groups 1 KiB (SBO)
+          const uint64_t adesc = smem_desc_sw128(sa + h * 2 * kTcBoxBytes, kTcBoxBytes, 1024);
+          umma_f16(tmem + static_cast<uint32_t>(h * kTcXRows), adesc, bdesc, idesc, t > 0 ? 1u : 0u);
+        }
+        umma_commit(&empty_bar[stage]);
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(args.status, G16_ERR_TIMEOUT);
+      }
+      umma_commit(done_bar);  // also the drain: arrives once every issued MMA has completed
+      mbar_wait(done_bar, 0, nullptr);  // TMEM is released below only after this
+    }
+  } else {
+    // ---------------- warps 0-3: build xhl, then the epilogue ----------------
+    const TX* x = static_cast<const TX*>(args.x);
+    // 1. per-row |max| over this CTA's chunk
+    float am[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) am[m] = 0.f;
+    for (int k = tid; k < nrows; k += 128)
+#pragma unroll
+      for (int m = 0; m < M; ++m) am[m] = fmaxf(am[m], fabsf(to_f32(x[static_cast<size_t>(m) * args.K + kb + k])));
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) am[m] = fmaxf(am[m], __shfl_xor_sync(0xffffffffu, am[m], o));
+      if (lane == 0) amax_w[warp * 8 + m] = am[m];
+    }
+    epi_sync();
+    float sc[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const float a = fmaxf(fmaxf(amax_w[m], amax_w[8 + m]), fmaxf(amax_w[16 + m], amax_w[24 + m]));
+      float inv;
+      sc[m] = split_scale(a, &inv);
+      if (tid == 0) scale_inv[m] = inv;
+    }
+    // 2. xhl rows: r < 8 -> hi of x row r, 8 <= r < 16 -> lo of x row r - 8 (zero past M / past the
+    //    chunk); 16-byte chunks of 8 k values, 128-byte swizzle (chunk index ^ (row & 7)).
+    const int nchunks = kTcXRows * nkb * 8;
+    for (int c = tid; c < nchunks; c += 128) {
+      const int r = c / (nkb * 8);
+      const int kc = c - r * (nkb * 8);  // 16-byte chunk index along K
+      const int m = r & 7;
+      const bool lo_row = r >= 8;
+      uint32_t packed[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v2[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int k = kc * 8 + 2 * j + q;
+          float v = 0.f;
+          if (m < M && k < nrows) {
+            float scale = 1.f;
+#pragma unroll
+            for (int mm = 0; mm < M; ++mm)
+              if (mm == m) scale = sc[mm];
+            const float xs = to_f32(x[static_cast<size_t>(m) * args.K + kb + k]) * scale;
+            const float hi = __half2float(__float2half_rn(xs));
+            v = lo_row ? xs - hi : hi;
+          }
+          v2[q] = v;
+        }
+        const __half2 h2 = __floats2half2_rn(v2[0], v2[1]);
+        packed[j] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      const int blk = kc >> 3, cin = kc & 7;
+      uint8_t* dst = xhl + blk * kTcXBlockBytes + (r >> 3) * 1024 + (r & 7) * 128 + ((cin ^ (r & 7)) << 4);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+    fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+    epi_sync();
+    if (tid == 0) mbar_arrive(xready_bar);
+
+    // 3. epilogue: wait for the last MMA, read the two [128 x 16] accumulators
+    bool got = mbar_wait(done_bar, 0, abort_flag);
+    got = __all_sync(0xffffffffu, got);
+    if (!got && lane == 0) {
+      *abort_flag = 1;
+      atomicExch(args.status, G16_ERR_TIMEOUT);
+    }
+    tc_fence_after();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t d[16];
+      __syncwarp();
+      tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(h * kTcXRows), d);
+      tmem_ld_wait();
+      const int col = h * 128 + warp * 32 + lane;
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const float v = (nstages > 0 && got) ? (__uint_as_float(d[m]) + __uint_as_float(d[8 + m])) * scale_inv[m] : 0.f;
+        part[m * kStrip + col] = v;
+      }
+    }
+  }
+
+  // Reduce across the cluster in rank order; CTA `rank` finalises a contiguous share of outputs.
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp < 4) {
+    const int total = M * kStrip;
+    const int share = (total + csize - 1) / csize;
+    const int i0 = rank * share;
+    const int i1 = min(total, i0 + share);
+    const uint32_t part_addr = smem_u32(part);
+    for (int i = i0 + tid; i < i1; i += 128) {
+      const int m = i / kStrip, c = i - m * kStrip;
+      const int n = n0 + c;
+      if (n < args.N) {
+        float pv[kMaxCluster];
+#pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q)
+          pv[q] = q < csize ? ld_cluster_f32(map_cluster(part_addr + 4u * i, q)) : 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q)
+          if (q < csize) acc += pv[q];
+        if (args.bias != nullptr) acc += args.bias[n];
+        if constexpr (OUT_F16) {
+          reinterpret_cast<__half*>(args.out)[static_cast<size_t>(m) * args.N + n] = __float2half_rn(acc);
+        } else {
+          reinterpret_cast<float*>(args.out)[static_cast<size_t>(m) * args.N + n] = acc;
+        }
+      }
+    }
+  }
+  cluster_sync();  // keep `part` alive until every peer has read it
+  if (warp == 4) {
+    __syncwarp();
+    tmem_dealloc(tmem, kTcTmemCols);
+  }
+}
+
+size_t skinny_tc_smem_bytes(int M, int kchunk) {
+  const int nkb = (kchunk + 63) / 64;
+  return 1024 + static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(nkb) * kTcXBlockBytes +
+         static_cast<size_t>(M) * kStrip * 4 + 32 * 4 + 8 * 4 + (2 * kStages + 2) * 8 + 8;
+}
+
+constexpr int kTcSmemAttrBytes = 1024 + kStages * kStageBytes + (kTcMaxChunk / 64) * kTcXBlockBytes +
+                                 8 * kStrip * 4 + 32 * 4 + 8 * 4 + (2 * kStages + 2) * 8 + 8;
+
+// Same cluster plan as the FMA variant, re-checked for residency with this kernel's footprint.
+template <typename F>
+int plan_tc_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan* out) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, SkinnyPlan> cache;
+  int devid = 0;
+  cudaError_t e = cudaGetDevice(&devid);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const uint64_t key = (static_cast<uint64_t>(devid) << 58) ^ (static_cast<uint64_t>(M) << 54) ^
+                       (static_cast<uint64_t>(K) << 27) ^ static_cast<uint64_t>(N);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return G16_OK;
+    }
+  }
+  SkinnyPlan p = plan_skinny(M, K, N, dev.sm_count);
+  p.smem_bytes = skinny_tc_smem_bytes(M, p.kchunk);
+  while (true) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(p, nullptr, attr);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    int active = 0;
+    e = cudaOccupancyMaxActiveClusters(&active, kern, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (active >= p.strips || p.csize == 1) break;
+    const int c = p.csize - 1;
+    p = plan_skinny(M, K, N, c * p.strips);
+    p.smem_bytes = skinny_tc_smem_bytes(M, p.kchunk);
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = p;
+  *out = p;
+  return G16_OK;
+}
+
+template <int M, typename TX, bool OUT_F16>
+int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void* out, int K, int N, cudaStream_t s,
+                       const DeviceInfo& dev) {
+  static std::atomic<uint64_t> attr_done{0};
+  auto kern = skinny_tc_kernel<M, TX, OUT_F16>;
+  cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
+  if (e != cudaSuccess) return cuda_fail(e);
+  SkinnyPlan p;
+  int st = plan_tc_for(kern, M, K, N, dev, &p);
+  if (st != G16_OK) return st;
+  if (p.kchunk > kTcMaxChunk) return launch_skinny_fma_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev);
+  if (p.smem_bytes != skinny_tc_smem_bytes(M, p.kchunk) ||
+      p.smem_bytes > static_cast<size_t>(kTcSmemAttrBytes))
+    return G16_ERR_ARG;
+  CUtensorMap tmap;
+  st = make_tmap_2d(&tmap, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                    kBoxRows, kTcBoxCols, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != G16_OK) return st;
+  SkinnyArgs a{};
+  a.x = x;
+  a.bias = bias;
+  a.out = out;
+  a.status = device_status_ptr();
+  if (a.status == nullptr) return G16_ERR_CUDA;
+  a.K = K;
+  a.N = N;
+  a.kchunk = p.kchunk;
+  a.piece = p.kchunk;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_cfg(p, s, attr);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, a);
+  if (e != cudaSuccess) return cuda_fail(e);
+  note_launch();
+  return G16_OK;
+}
+
+// The tensor-core variant whenever its K chunk fits in shared memory, else the FMA variant.
+template <int M, typename TX, bool OUT_F16>
+int launch_skinny_t(const void* x, const uint16_t* w, const float* bias, void* out, int K, int N, cudaStream_t s,
+                    const DeviceInfo& dev) {
+  return launch_skinny_tc_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev);
 }
 
 template <int M>
