@@ -434,6 +434,7 @@ constexpr int kTcXRows = 16;     // UMMA N: x_hi rows 0..7, x_lo rows 8..15
 constexpr int kTcXBlockBytes = kTcXRows * 128;          // one 64-wide K block of xhl (2 KiB)
 constexpr int kTcMaxChunk = 2048;                       // xhl <= 64 KiB of shared memory
 constexpr uint32_t kTcTmemCols = 32;                    // two [128 x 16] fp32 accumulators
+constexpr int kTcBatch = 4;                             // x values per row and thread in flight
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
@@ -562,20 +563,34 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   } else {
     // ---------------- warps 0-3: build xhl, then the epilogue ----------------
     const TX* x = static_cast<const TX*>(args.x);
-    // 1. per-row |max| over this CTA's chunk
+    // 0. zero xhl: rows >= M (hi and lo) and k >= nrows must contribute nothing
+    for (int i = tid; i < nkb * (kTcXBlockBytes / 16); i += 128)
+      reinterpret_cast<uint4*>(xhl)[i] = make_uint4(0u, 0u, 0u, 0u);
+    // 1. per-row |max| over this CTA's chunk; kTcBatch k values per thread in flight at once
     float am[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) am[m] = 0.f;
-    for (int k = tid; k < nrows; k += 128)
+    for (int k0 = tid; k0 < nrows; k0 += 128 * kTcBatch) {
+      float v[M][kTcBatch];
 #pragma unroll
-      for (int m = 0; m < M; ++m) am[m] = fmaxf(am[m], fabsf(to_f32(x[static_cast<size_t>(m) * args.K + kb + k])));
+      for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int u = 0; u < kTcBatch; ++u) {
+          const int k = k0 + u * 128;
+          v[m][u] = k < nrows ? to_f32(x[static_cast<size_t>(m) * args.K + kb + k]) : 0.f;
+        }
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int u = 0; u < kTcBatch; ++u) am[m] = fmaxf(am[m], fabsf(v[m][u]));
+    }
 #pragma unroll
     for (int m = 0; m < M; ++m) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) am[m] = fmaxf(am[m], __shfl_xor_sync(0xffffffffu, am[m], o));
       if (lane == 0) amax_w[warp * 8 + m] = am[m];
     }
-    epi_sync();
+    epi_sync();  // amax_w complete, xhl zeroed
     float sc[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
@@ -584,39 +599,34 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       sc[m] = split_scale(a, &inv);
       if (tid == 0) scale_inv[m] = inv;
     }
-    // 2. xhl rows: r < 8 -> hi of x row r, 8 <= r < 16 -> lo of x row r - 8 (zero past M / past the
-    //    chunk); 16-byte chunks of 8 k values, 128-byte swizzle (chunk index ^ (row & 7)).
-    const int nchunks = kTcXRows * nkb * 8;
-    for (int c = tid; c < nchunks; c += 128) {
-      const int r = c / (nkb * 8);
-      const int kc = c - r * (nkb * 8);  // 16-byte chunk index along K
-      const int m = r & 7;
-      const bool lo_row = r >= 8;
-      uint32_t packed[4];
+    // 2. x*s = hi + lo into xhl (row m: hi, row 8 + m: lo), 128-byte swizzled K-major layout; the
+    //    reloads hit L1.
+    for (int k0 = tid; k0 < nrows; k0 += 128 * kTcBatch) {
+      float v[M][kTcBatch];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float v2[2];
+      for (int m = 0; m < M; ++m)
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int k = kc * 8 + 2 * j + q;
-          float v = 0.f;
-          if (m < M && k < nrows) {
-            float scale = 1.f;
-#pragma unroll
-            for (int mm = 0; mm < M; ++mm)
-              if (mm == m) scale = sc[mm];
-            const float xs = to_f32(x[static_cast<size_t>(m) * args.K + kb + k]) * scale;
-            const float hi = __half2float(__float2half_rn(xs));
-            v = lo_row ? xs - hi : hi;
-          }
-          v2[q] = v;
+        for (int u = 0; u < kTcBatch; ++u) {
+          const int k = k0 + u * 128;
+          v[m][u] = k < nrows ? to_f32(x[static_cast<size_t>(m) * args.K + kb + k]) : 0.f;
         }
-        const __half2 h2 = __floats2half2_rn(v2[0], v2[1]);
-        packed[j] = *reinterpret_cast<const uint32_t*>(&h2);
+#pragma unroll
+      for (int u = 0; u < kTcBatch; ++u) {
+        const int k = k0 + u * 128;
+        if (k < nrows) {
+          uint8_t* kbase = xhl + (k >> 6) * kTcXBlockBytes + ((k & 7) << 1);
+          const int kchunk16 = (k & 63) >> 3;
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            const float xs = v[m][u] * sc[m];
+            const __half hi = __float2half_rn(xs);
+            const __half lo = __float2half_rn(xs - __half2float(hi));
+            const int rh = m, rl = 8 + m;
+            *reinterpret_cast<__half*>(kbase + (rh >> 3) * 1024 + (rh & 7) * 128 + ((kchunk16 ^ (rh & 7)) << 4)) = hi;
+            *reinterpret_cast<__half*>(kbase + (rl >> 3) * 1024 + (rl & 7) * 128 + ((kchunk16 ^ (rl & 7)) << 4)) = lo;
+          }
+        }
       }
-      const int blk = kc >> 3, cin = kc & 7;
-      uint8_t* dst = xhl + blk * kTcXBlockBytes + (r >> 3) * 1024 + (r & 7) * 128 + ((cin ^ (r & 7)) << 4);
-      *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     }
     fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
     epi_sync();
