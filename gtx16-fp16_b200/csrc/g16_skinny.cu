@@ -427,12 +427,14 @@ int launch_skinny_fma_t(const void* x, const uint16_t* w, const float* bias, voi
 // partial for (m, n) is (D[n][m] + D[n][m+8]) / s, then K chunks are reduced across the cluster
 // as in the FMA variant. Work per stage is two MMAs whatever M is.
 // =============================================================================================
+constexpr int kTcStages = 8;                            // 64 KiB of weights in flight per CTA
+constexpr int kTcStageBytes = kStageBytes;              // [16 rows x 256 columns] = 8 KiB
 constexpr int kTcBoxCols = 64;                          // one 128-byte swizzle row of fp16
 constexpr int kTcBoxBytes = kBoxRows * kTcBoxCols * 2;  // 2 KiB
 constexpr int kTcThreads = 192;  // warps 0-3: x prep + epilogue, warp 4: TMEM + MMA, warp 5: TMA
 constexpr int kTcXRows = 16;     // UMMA N: x_hi rows 0..7, x_lo rows 8..15
 constexpr int kTcXBlockBytes = kTcXRows * 128;          // one 64-wide K block of xhl (2 KiB)
-constexpr int kTcMaxChunk = 2048;                       // xhl <= 64 KiB of shared memory
+constexpr int kTcMaxChunk = 1024;                       // xhl <= 32 KiB: two CTAs fit per SM
 constexpr uint32_t kTcTmemCols = 32;                    // two [128 x 16] fp32 accumulators
 constexpr int kTcBatch = 4;                             // x values per row and thread in flight
 
@@ -452,15 +454,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* ring = smem;                                           // kStages x [4 boxes of 16 x 64]
+  uint8_t* ring = smem;                                           // kTcStages x [4 boxes of 16 x 64]
   const int nkb = (args.kchunk + 63) / 64;                        // 64-wide K blocks of x
-  uint8_t* xhl = ring + kStages * kStageBytes;                    // nkb x 2 KiB, 1 KiB aligned
+  uint8_t* xhl = ring + kTcStages * kTcStageBytes;                    // nkb x 2 KiB, 1 KiB aligned
   float* part = reinterpret_cast<float*>(xhl + nkb * kTcXBlockBytes);  // [M][kStrip]
   float* amax_w = part + M * kStrip;                              // [4 warps][8]
   float* scale_inv = amax_w + 32;                                 // [8]
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(scale_inv + 8);
-  uint64_t* empty_bar = full_bar + kStages;
-  uint64_t* xready_bar = empty_bar + kStages;
+  uint64_t* empty_bar = full_bar + kTcStages;
+  uint64_t* xready_bar = empty_bar + kTcStages;
   uint64_t* done_bar = xready_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -484,7 +486,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   const int nstages = (nrows + kBoxRows - 1) / kBoxRows;
 
   if (tid == 0) {
-    for (int st = 0; st < kStages; ++st) {
+    for (int st = 0; st < kTcStages; ++st) {
       mbar_init(&full_bar[st], 1);
       mbar_init(&empty_bar[st], 1);
     }
@@ -508,25 +510,25 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       tma_prefetch_desc(&tmap_w);
       uint32_t phase = 0;
       int stage = 0;
-      bool armed[kStages];
-      uint32_t armed_phase[kStages];
-      for (int st = 0; st < kStages; ++st) { armed[st] = false; armed_phase[st] = 0; }
+      bool armed[kTcStages];
+      uint32_t armed_phase[kTcStages];
+      for (int st = 0; st < kTcStages; ++st) { armed[st] = false; armed_phase[st] = 0; }
       bool ok = true;
       for (int t = 0; t < nstages; ++t) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
-        uint8_t* dst = ring + stage * kStageBytes;
-        mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+        uint8_t* dst = ring + stage * kTcStageBytes;
+        mbar_arrive_expect_tx(&full_bar[stage], kTcStageBytes);
         armed[stage] = true;
         armed_phase[stage] = phase;
 #pragma unroll
         for (int j = 0; j < kStrip / kTcBoxCols; ++j)
           tma_load_2d(dst + j * kTcBoxBytes, &tmap_w, &full_bar[stage], n0 + j * kTcBoxCols, kb + t * kBoxRows);
-        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
       }
       if (!ok) {
         *abort_flag = 1;
         atomicExch(args.status, G16_ERR_TIMEOUT);
-        for (int st = 0; st < kStages; ++st)
+        for (int st = 0; st < kTcStages; ++st)
           if (armed[st]) mbar_wait(&full_bar[st], armed_phase[st], nullptr);
       }
     }
@@ -541,7 +543,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       for (int t = 0; t < nstages && ok; ++t) {
         if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sa = smem_u32(ring + stage * kStageBytes);
+        const uint32_t sa = smem_u32(ring + stage * kTcStageBytes);
         const uint32_t sb = smem_u32(xhl) + (t >> 2) * kTcXBlockBytes + (t & 3) * 32;
         const uint64_t bdesc = smem_desc_sw128(sb, 16, 1024);
 #pragma unroll
@@ -551,7 +553,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
           umma_f16(tmem + static_cast<uint32_t>(h * kTcXRows), adesc, bdesc, idesc, t > 0 ? 1u : 0u);
         }
         umma_commit(&empty_bar[stage]);
-        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
       }
       if (!ok) {
         *abort_flag = 1;
@@ -695,12 +697,12 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
 
 size_t skinny_tc_smem_bytes(int M, int kchunk) {
   const int nkb = (kchunk + 63) / 64;
-  return 1024 + static_cast<size_t>(kStages) * kStageBytes + static_cast<size_t>(nkb) * kTcXBlockBytes +
-         static_cast<size_t>(M) * kStrip * 4 + 32 * 4 + 8 * 4 + (2 * kStages + 2) * 8 + 8;
+  return 1024 + static_cast<size_t>(kTcStages) * kTcStageBytes + static_cast<size_t>(nkb) * kTcXBlockBytes +
+         static_cast<size_t>(M) * kStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
 }
 
-constexpr int kTcSmemAttrBytes = 1024 + kStages * kStageBytes + (kTcMaxChunk / 64) * kTcXBlockBytes +
-                                 8 * kStrip * 4 + 32 * 4 + 8 * 4 + (2 * kStages + 2) * 8 + 8;
+constexpr int kTcSmemAttrBytes = 1024 + kTcStages * kTcStageBytes + (kTcMaxChunk / 64) * kTcXBlockBytes +
+                                 8 * kStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
 
 // Same cluster plan as the FMA variant, re-checked for residency with this kernel's footprint.
 template <typename F>
