@@ -264,6 +264,14 @@ int g16_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype,
                      static_cast<cudaStream_t>(stream), *dev);
 }
 
+int g16_skinny_plan(int M, int K, int N, int x_dtype, int* info) {
+  if (info == nullptr || K <= 0 || N <= 0 || (x_dtype != G16_F32 && x_dtype != G16_F16)) return G16_ERR_ARG;
+  int st = G16_OK;
+  const DeviceInfo* dev = device_info(&st);
+  if (dev == nullptr) return st;
+  return skinny_plan_info(M, K, N, x_dtype, info, *dev);
+}
+
 int g16_device_status(int* status_out, int clear, void* stream) {
   if (status_out == nullptr) return G16_ERR_ARG;
   int* p = device_status_ptr();

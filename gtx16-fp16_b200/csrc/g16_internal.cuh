@@ -32,6 +32,11 @@ void note_launch(uint64_t n = 1);
 int launch_skinny(const void* x, int x_dtype, const uint16_t* w, const float* bias, void* out, int out_dtype, int M,
                   int K, int N, cudaStream_t s, const DeviceInfo& dev);
 
+// Launch plan of the skinny kernel for (M, K, N): info[0] tensor-core variant (1) or FMA (0),
+// [1] cluster size, [2] strips, [3] K chunk, [4] dynamic shared memory, [5] resident clusters at the
+// first cluster size tried, [6] at the chosen one.
+int skinny_plan_info(int M, int K, int N, int x_dtype, int* info, const DeviceInfo& dev);
+
 int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M, int K, float thresh,
                     cudaStream_t s);
 

@@ -279,6 +279,9 @@ skinny_fma_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs a
 struct SkinnyPlan {
   int csize, strips, kchunk, piece;
   size_t smem_bytes;
+  int active_first = -1;  // resident clusters at the first cluster size tried
+  int active = -1;        // resident clusters at the chosen cluster size
+  int tc = 0;             // 1: tensor-core variant
 };
 
 size_t skinny_smem_bytes(int M, int piece) {
@@ -318,6 +321,9 @@ cudaError_t ensure_attrs(F* kern, std::atomic<uint64_t>& done, int smem) {
   if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  // Carve the whole unified L1 as shared memory, so two CTAs (and cluster peers) fit per SM.
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
   return e;
 }
@@ -421,26 +427,32 @@ int launch_skinny_fma_t(const void* x, const uint16_t* w, const float* bias, voi
 // |max| lands in [2^14, 2^15)), splits x*s = hi + lo into two fp16 values (hi = fp16(x*s),
 // lo = fp16(x*s - hi); hi + lo carries 22 significant bits, products with fp16 weights are exact,
 // sums are fp32), and computes out^T[n][m'] = sum_k W[k][n] * xhl[m'][k] with
-// tcgen05.mma kind::f16, M=128 (weight columns), N=16 (m' < 8: hi rows, m' >= 8: lo rows), K=16
-// per 16-row stage. W is the MN-major A operand, streamed by TMA in the same 128-byte swizzled
-// layout the GEMM uses for its B operand; xhl is a K-major B operand built in shared memory. The
-// partial for (m, n) is (D[n][m] + D[n][m+8]) / s, then K chunks are reduced across the cluster
-// as in the FMA variant. Work per stage is two MMAs whatever M is.
+// tcgen05.mma kind::f16, M=128 (weight columns), N=16 (m' < 8: hi rows, m' >= 8: lo rows), K=16.
+// W is the MN-major A operand, streamed by TMA in 128-byte swizzled [32 rows x 64 columns] boxes
+// (the layout the GEMM uses for its B operand); xhl is a K-major B operand built in shared memory.
+// The partial for (m, n) is (D[n][m] + D[n][m+8]) / s; K chunks are then reduced across the
+// cluster in rank order as in the FMA variant. Work per 32-row stage is two MMAs whatever M is.
+//
+// A kernel that allocates tensor memory runs one CTA per SM, and a cluster must fit inside one
+// GPC, so strips are 128 columns wide (4096 columns -> 32 clusters of 4 CTAs on 148 SMs) rather
+// than the FMA variant's 256.
 // =============================================================================================
-constexpr int kTcStages = 8;                            // 64 KiB of weights in flight per CTA
-constexpr int kTcStageBytes = kStageBytes;              // [16 rows x 256 columns] = 8 KiB
+constexpr int kTcStrip = 128;                           // output columns per cluster (UMMA M)
+constexpr int kTcRows = 32;                             // weight rows per stage
+constexpr int kTcStages = 12;                           // 96 KiB of weights in flight per CTA
 constexpr int kTcBoxCols = 64;                          // one 128-byte swizzle row of fp16
-constexpr int kTcBoxBytes = kBoxRows * kTcBoxCols * 2;  // 2 KiB
+constexpr int kTcBoxBytes = kTcRows * kTcBoxCols * 2;   // 4 KiB
+constexpr int kTcStageBytes = 2 * kTcBoxBytes;          // [32 rows x 128 columns] = 8 KiB
 constexpr int kTcThreads = 192;  // warps 0-3: x prep + epilogue, warp 4: TMEM + MMA, warp 5: TMA
 constexpr int kTcXRows = 16;     // UMMA N: x_hi rows 0..7, x_lo rows 8..15
 constexpr int kTcXBlockBytes = kTcXRows * 128;          // one 64-wide K block of xhl (2 KiB)
-constexpr int kTcMaxChunk = 1024;                       // xhl <= 32 KiB: two CTAs fit per SM
-constexpr uint32_t kTcTmemCols = 32;                    // two [128 x 16] fp32 accumulators
+constexpr int kTcMaxChunk = 2048;                       // xhl <= 64 KiB of shared memory
+constexpr uint32_t kTcTmemCols = 32;                    // one [128 x 16] fp32 accumulator (minimum allocation)
 constexpr int kTcBatch = 4;                             // x values per row and thread in flight
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
-// Power-of-two scale that maps |max| into [2^14, 2^15) (1 for zero rows); writes its reciprocal.
+// Power-of-two scale that maps |max| into [2^14, 2^15) (2^125 for zero rows); writes its reciprocal.
 __device__ __forceinline__ float split_scale(float amax, float* inv) {
   const int ef = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu);  // biased exponent
   int e = 141 - ef;                                                       // 15 - unbiased(frexp)
@@ -454,11 +466,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* ring = smem;                                           // kTcStages x [4 boxes of 16 x 64]
+  uint8_t* ring = smem;                                           // kTcStages x [2 boxes of 32 x 64]
   const int nkb = (args.kchunk + 63) / 64;                        // 64-wide K blocks of x
-  uint8_t* xhl = ring + kTcStages * kTcStageBytes;                    // nkb x 2 KiB, 1 KiB aligned
-  float* part = reinterpret_cast<float*>(xhl + nkb * kTcXBlockBytes);  // [M][kStrip]
-  float* amax_w = part + M * kStrip;                              // [4 warps][8]
+  uint8_t* xhl = ring + kTcStages * kTcStageBytes;                // nkb x 2 KiB, 1 KiB aligned
+  float* part = reinterpret_cast<float*>(xhl + nkb * kTcXBlockBytes);  // [M][kTcStrip]
+  float* amax_w = part + M * kTcStrip;                            // [4 warps][8]
   float* scale_inv = amax_w + 32;                                 // [8]
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(scale_inv + 8);
   uint64_t* empty_bar = full_bar + kTcStages;
@@ -479,11 +491,11 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   const int lane = tid & 31;
   const int rank = blockIdx.x;
   const int csize = gridDim.x;
-  const int n0 = blockIdx.y * kStrip;
+  const int n0 = blockIdx.y * kTcStrip;
   const int kb = rank * args.kchunk;
   const int ke = min(args.K, kb + args.kchunk);
   const int nrows = max(0, ke - kb);
-  const int nstages = (nrows + kBoxRows - 1) / kBoxRows;
+  const int nstages = (nrows + kTcRows - 1) / kTcRows;
 
   if (tid == 0) {
     for (int st = 0; st < kTcStages; ++st) {
@@ -521,8 +533,8 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
         armed[stage] = true;
         armed_phase[stage] = phase;
 #pragma unroll
-        for (int j = 0; j < kStrip / kTcBoxCols; ++j)
-          tma_load_2d(dst + j * kTcBoxBytes, &tmap_w, &full_bar[stage], n0 + j * kTcBoxCols, kb + t * kBoxRows);
+        for (int j = 0; j < kTcStrip / kTcBoxCols; ++j)
+          tma_load_2d(dst + j * kTcBoxBytes, &tmap_w, &full_bar[stage], n0 + j * kTcBoxCols, kb + t * kTcRows);
         if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
       }
       if (!ok) {
@@ -535,7 +547,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   } else if (warp == 4) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      // D[n][m'] += W[k][n] * xhl[m'][k]: A = W (MN-major), B = xhl (K-major), M=128, N=16.
+      // D[n][m'] += W[k][n] * xhl[m'][k]: A = W (MN-major), B = xhl (K-major), M=128, N=16, K=16.
       constexpr uint32_t idesc = idesc_f16_f32(128, kTcXRows, /*b_mn_major=*/false, /*a_mn_major=*/true);
       bool ok = mbar_wait(xready_bar, 0, abort_flag);
       uint32_t phase = 0;
@@ -544,13 +556,14 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
         if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(ring + stage * kTcStageBytes);
-        const uint32_t sb = smem_u32(xhl) + (t >> 2) * kTcXBlockBytes + (t & 3) * 32;
-        const uint64_t bdesc = smem_desc_sw128(sb, 16, 1024);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          // columns [128h, 128h + 128): two 64-column boxes, 2 KiB apart (LBO); 8-row k groups 1 KiB (SBO)
-          const uint64_t adesc = smem_desc_sw128(sa + h * 2 * kTcBoxBytes, kTcBoxBytes, 1024);
-          umma_f16(tmem + static_cast<uint32_t>(h * kTcXRows), adesc, bdesc, idesc, t > 0 ? 1u : 0u);
+        for (int j = 0; j < kTcRows / kUmmaK; ++j) {
+          const int ks = t * (kTcRows / kUmmaK) + j;  // 16-wide K step within the chunk
+          // A: rows [16j, 16j + 16) of the stage: 2 KiB in; two 64-column boxes 4 KiB apart (LBO),
+          // 8-row k groups 1 KiB apart (SBO). B: K step ks of xhl.
+          const uint64_t adesc = smem_desc_sw128(sa + j * (kUmmaK * 128), kTcBoxBytes, 1024);
+          const uint64_t bdesc = smem_desc_sw128(smem_u32(xhl) + (ks >> 2) * kTcXBlockBytes + (ks & 3) * 32, 16, 1024);
+          umma_f16(tmem, adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
         }
         umma_commit(&empty_bar[stage]);
         if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
@@ -634,7 +647,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
     epi_sync();
     if (tid == 0) mbar_arrive(xready_bar);
 
-    // 3. epilogue: wait for the last MMA, read the two [128 x 16] accumulators
+    // 3. epilogue: wait for the last MMA, read the [128 x 16] accumulator (lane = weight column)
     bool got = mbar_wait(done_bar, 0, abort_flag);
     got = __all_sync(0xffffffffu, got);
     if (!got && lane == 0) {
@@ -642,18 +655,15 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       atomicExch(args.status, G16_ERR_TIMEOUT);
     }
     tc_fence_after();
+    uint32_t d[16];
+    __syncwarp();
+    tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(warp * 32) << 16), d);
+    tmem_ld_wait();
+    const int col = warp * 32 + lane;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t d[16];
-      __syncwarp();
-      tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(h * kTcXRows), d);
-      tmem_ld_wait();
-      const int col = h * 128 + warp * 32 + lane;
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        const float v = (nstages > 0 && got) ? (__uint_as_float(d[m]) + __uint_as_float(d[8 + m])) * scale_inv[m] : 0.f;
-        part[m * kStrip + col] = v;
-      }
+    for (int m = 0; m < M; ++m) {
+      const float v = (nstages > 0 && got) ? (__uint_as_float(d[m]) + __uint_as_float(d[8 + m])) * scale_inv[m] : 0.f;
+      part[m * kTcStrip + col] = v;
     }
   }
 
@@ -662,13 +672,13 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   cluster_sync();
   tc_fence_after();
   if (warp < 4) {
-    const int total = M * kStrip;
+    const int total = M * kTcStrip;
     const int share = (total + csize - 1) / csize;
     const int i0 = rank * share;
     const int i1 = min(total, i0 + share);
     const uint32_t part_addr = smem_u32(part);
     for (int i = i0 + tid; i < i1; i += 128) {
-      const int m = i / kStrip, c = i - m * kStrip;
+      const int m = i / kTcStrip, c = i - m * kTcStrip;
       const int n = n0 + c;
       if (n < args.N) {
         float pv[kMaxCluster];
@@ -698,13 +708,34 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
 size_t skinny_tc_smem_bytes(int M, int kchunk) {
   const int nkb = (kchunk + 63) / 64;
   return 1024 + static_cast<size_t>(kTcStages) * kTcStageBytes + static_cast<size_t>(nkb) * kTcXBlockBytes +
-         static_cast<size_t>(M) * kStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
+         static_cast<size_t>(M) * kTcStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
 }
 
 constexpr int kTcSmemAttrBytes = 1024 + kTcStages * kTcStageBytes + (kTcMaxChunk / 64) * kTcXBlockBytes +
-                                 8 * kStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
+                                 8 * kTcStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
 
-// Same cluster plan as the FMA variant, re-checked for residency with this kernel's footprint.
+// Column strips of kTcStrip; K split over up to 16 cluster ranks with chunks that are whole stages.
+SkinnyPlan plan_tc(int M, int K, int N, int ctas) {
+  SkinnyPlan p{};
+  p.strips = (N + kTcStrip - 1) / kTcStrip;
+  int c = ctas / p.strips;
+  if (c < 1) c = 1;
+  if (c > kMaxCluster) c = kMaxCluster;
+  const int max_by_k = K / (2 * kTcRows) > 0 ? K / (2 * kTcRows) : 1;
+  if (c > max_by_k) c = max_by_k;
+  int kchunk = (K + c - 1) / c;
+  kchunk = (kchunk + kTcRows - 1) / kTcRows * kTcRows;
+  c = (K + kchunk - 1) / kchunk;
+  if (c < 1) c = 1;
+  p.csize = c;
+  p.kchunk = kchunk;
+  p.piece = kchunk;
+  p.smem_bytes = skinny_tc_smem_bytes(M, kchunk);
+  p.tc = kchunk <= kTcMaxChunk ? 1 : 0;
+  return p;
+}
+
+// The largest cluster whose clusters are all resident at once (one CTA per SM with tensor memory).
 template <typename F>
 int plan_tc_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan* out) {
   static std::mutex mu;
@@ -722,20 +753,21 @@ int plan_tc_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan*
       return G16_OK;
     }
   }
-  SkinnyPlan p = plan_skinny(M, K, N, dev.sm_count);
-  p.smem_bytes = skinny_tc_smem_bytes(M, p.kchunk);
-  while (true) {
+  SkinnyPlan p = plan_tc(M, K, N, dev.sm_count);
+  int first = -1;
+  while (p.tc) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(p, nullptr, attr);
     cfg.blockDim = dim3(kTcThreads, 1, 1);
     int active = 0;
     e = cudaOccupancyMaxActiveClusters(&active, kern, &cfg);
     if (e != cudaSuccess) return cuda_fail(e);
+    if (first < 0) first = active;
+    p.active = active;
     if (active >= p.strips || p.csize == 1) break;
-    const int c = p.csize - 1;
-    p = plan_skinny(M, K, N, c * p.strips);
-    p.smem_bytes = skinny_tc_smem_bytes(M, p.kchunk);
+    p = plan_tc(M, K, N, (p.csize - 1) * p.strips);
   }
+  p.active_first = first;
   std::lock_guard<std::mutex> lk(mu);
   cache[key] = p;
   *out = p;
@@ -752,13 +784,12 @@ int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void
   SkinnyPlan p;
   int st = plan_tc_for(kern, M, K, N, dev, &p);
   if (st != G16_OK) return st;
-  if (p.kchunk > kTcMaxChunk) return launch_skinny_fma_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev);
-  if (p.smem_bytes != skinny_tc_smem_bytes(M, p.kchunk) ||
-      p.smem_bytes > static_cast<size_t>(kTcSmemAttrBytes))
+  if (!p.tc) return launch_skinny_fma_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev);
+  if (p.smem_bytes != skinny_tc_smem_bytes(M, p.kchunk) || p.smem_bytes > static_cast<size_t>(kTcSmemAttrBytes))
     return G16_ERR_ARG;
   CUtensorMap tmap;
   st = make_tmap_2d(&tmap, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
-                    kBoxRows, kTcBoxCols, CU_TENSOR_MAP_SWIZZLE_128B);
+                    kTcRows, kTcBoxCols, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
   SkinnyArgs a{};
   a.x = x;
@@ -812,6 +843,34 @@ int launch_skinny(const void* x, int x_dtype, const uint16_t* w, const float* bi
     case 8: return dispatch_types<8>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
     default: return G16_ERR_ARG;
   }
+}
+
+int skinny_plan_info(int M, int K, int N, int x_dtype, int* info, const DeviceInfo& dev) {
+  if (M < 1 || M > 8) return G16_ERR_ARG;
+  SkinnyPlan p;
+  int st;
+  if (x_dtype == G16_F32) {
+    static std::atomic<uint64_t> attr_done{0};
+    auto kern = skinny_tc_kernel<1, float, false>;
+    cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
+    if (e != cudaSuccess) return cuda_fail(e);
+    st = plan_tc_for(kern, M, K, N, dev, &p);
+  } else {
+    static std::atomic<uint64_t> attr_done{0};
+    auto kern = skinny_tc_kernel<1, __half, false>;
+    cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
+    if (e != cudaSuccess) return cuda_fail(e);
+    st = plan_tc_for(kern, M, K, N, dev, &p);
+  }
+  if (st != G16_OK) return st;
+  info[0] = p.tc;
+  info[1] = p.csize;
+  info[2] = p.strips;
+  info[3] = p.kchunk;
+  info[4] = static_cast<int>(p.smem_bytes);
+  info[5] = p.active_first;
+  info[6] = p.active;
+  return G16_OK;
 }
 
 }  // namespace g16

@@ -34,6 +34,7 @@ SIGNATURES = {
     "g16_gemm_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g16_gemm_auto_ksplit": (_I, [_I, _I, _I]),
     "g16_gemm_static_scratch": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P]),
+    "g16_skinny_plan": (_I, [_I, _I, _I, _I, ctypes.POINTER(_I)]),
     "g16_device_status": (_I, [ctypes.POINTER(_I), _I, _P]),
     "g16_launch_count": (ctypes.c_uint64, []),
     "g16_strerror": (ctypes.c_char_p, [_I]),

@@ -115,6 +115,13 @@ int g16_gemm_auto_ksplit(int M, int K, int N);
 int g16_gemm_static_scratch(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                             const float* rscale, int M, int K, int N, int ksplit, void* stream);
 
+/* Launch plan the skinny path would use for (M, K, N) on the current device (introspection for
+ * tests and tuning; the reference has no equivalent, its plan is skinny_config, ops.py:45-51):
+ * info[0] = 1 tensor-core variant / 0 FMA variant, [1] cluster size (CTAs splitting K), [2] column
+ * strips, [3] K rows per CTA, [4] dynamic shared memory bytes, [5] clusters resident at once at the
+ * first cluster size tried, [6] at the chosen size. info must hold 7 ints. */
+int g16_skinny_plan(int M, int K, int N, int x_dtype, int* info);
+
 /* Device-side status word of the current device: G16_OK, or G16_ERR_TIMEOUT if a kernel's
  * bounded wait expired since the last clear. Synchronises `stream`. clear != 0 resets it. */
 int g16_device_status(int* status_out, int clear, void* stream);
