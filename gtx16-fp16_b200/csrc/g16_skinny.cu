@@ -439,7 +439,7 @@ int launch_skinny_fma_t(const void* x, const uint16_t* w, const float* bias, voi
 // =============================================================================================
 constexpr int kTcStrip = 128;                           // output columns per cluster (UMMA M)
 constexpr int kTcRows = 32;                             // weight rows per stage
-constexpr int kTcStages = 12;                           // 96 KiB of weights in flight per CTA
+constexpr int kTcStages = 10;                           // 80 KiB of weights in flight per CTA
 constexpr int kTcBoxCols = 64;                          // one 128-byte swizzle row of fp16
 constexpr int kTcBoxBytes = kTcRows * kTcBoxCols * 2;   // 4 KiB
 constexpr int kTcStageBytes = 2 * kTcBoxBytes;          // [32 rows x 128 columns] = 8 KiB
@@ -448,9 +448,23 @@ constexpr int kTcXRows = 16;     // UMMA N: x_hi rows 0..7, x_lo rows 8..15
 constexpr int kTcXBlockBytes = kTcXRows * 128;          // one 64-wide K block of xhl (2 KiB)
 constexpr int kTcMaxChunk = 2048;                       // xhl <= 64 KiB of shared memory
 constexpr uint32_t kTcTmemCols = 32;                    // one [128 x 16] fp32 accumulator (minimum allocation)
-constexpr int kTcBatch = 4;                             // x values per row and thread in flight
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+
+// Eight consecutive values from shared memory as fp32 (16-byte aligned source).
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
+  const uint4 u = reinterpret_cast<const uint4*>(p)[0];
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __half22float2(h[j]);
+    v[2 * j] = f.x; v[2 * j + 1] = f.y;
+  }
+}
 
 // Power-of-two scale that maps |max| into [2^14, 2^15) (2^125 for zero rows); writes its reciprocal.
 __device__ __forceinline__ float split_scale(float amax, float* inv) {
@@ -469,7 +483,8 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   uint8_t* ring = smem;                                           // kTcStages x [2 boxes of 32 x 64]
   const int nkb = (args.kchunk + 63) / 64;                        // 64-wide K blocks of x
   uint8_t* xhl = ring + kTcStages * kTcStageBytes;                // nkb x 2 KiB, 1 KiB aligned
-  float* part = reinterpret_cast<float*>(xhl + nkb * kTcXBlockBytes);  // [M][kTcStrip]
+  TX* xst = reinterpret_cast<TX*>(xhl + nkb * kTcXBlockBytes);    // [M][nkb * 64]: x chunk as loaded
+  float* part = reinterpret_cast<float*>(xst + M * nkb * 64);     // [M][kTcStrip]
   float* amax_w = part + M * kTcStrip;                            // [4 warps][8]
   float* scale_inv = amax_w + 32;                                 // [8]
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(scale_inv + 8);
@@ -578,26 +593,33 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   } else {
     // ---------------- warps 0-3: build xhl, then the epilogue ----------------
     const TX* x = static_cast<const TX*>(args.x);
-    // 0. zero xhl: rows >= M (hi and lo) and k >= nrows must contribute nothing
+    // 0. copy this CTA's x chunk into xst (one memory latency; zero past the chunk) and zero xhl
+    //    (rows >= M, hi and lo, must contribute nothing).
+    const int kpad = nkb * 64;
+    constexpr int kVec = 16 / static_cast<int>(sizeof(TX));      // elements per 16-byte copy
+    for (int i = tid; i < M * (kpad / kVec); i += 128) {
+      const int m = i / (kpad / kVec);
+      const int k = (i - m * (kpad / kVec)) * kVec;
+      const int valid = min(kVec, max(0, nrows - k));
+      const TX* src = x + static_cast<size_t>(m) * args.K + kb + (valid > 0 ? k : 0);
+      cp_async_16(xst + m * kpad + k, src, static_cast<uint32_t>(valid * sizeof(TX)));
+    }
     for (int i = tid; i < nkb * (kTcXBlockBytes / 16); i += 128)
       reinterpret_cast<uint4*>(xhl)[i] = make_uint4(0u, 0u, 0u, 0u);
-    // 1. per-row |max| over this CTA's chunk; kTcBatch k values per thread in flight at once
+    cp_async_wait_all();
+    epi_sync();
+    // 1. per-row |max| over the chunk (8 values per 16 bytes read)
     float am[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) am[m] = 0.f;
-    for (int k0 = tid; k0 < nrows; k0 += 128 * kTcBatch) {
-      float v[M][kTcBatch];
+    for (int k = tid * 8; k < kpad; k += 128 * 8) {
 #pragma unroll
-      for (int m = 0; m < M; ++m)
+      for (int m = 0; m < M; ++m) {
+        float v[8];
+        load8(xst + m * kpad + k, v);
 #pragma unroll
-        for (int u = 0; u < kTcBatch; ++u) {
-          const int k = k0 + u * 128;
-          v[m][u] = k < nrows ? to_f32(x[static_cast<size_t>(m) * args.K + kb + k]) : 0.f;
-        }
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int u = 0; u < kTcBatch; ++u) am[m] = fmaxf(am[m], fabsf(v[m][u]));
+        for (int j = 0; j < 8; ++j) am[m] = fmaxf(am[m], fabsf(v[j]));
+      }
     }
 #pragma unroll
     for (int m = 0; m < M; ++m) {
@@ -605,7 +627,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       for (int o = 16; o > 0; o >>= 1) am[m] = fmaxf(am[m], __shfl_xor_sync(0xffffffffu, am[m], o));
       if (lane == 0) amax_w[warp * 8 + m] = am[m];
     }
-    epi_sync();  // amax_w complete, xhl zeroed
+    epi_sync();  // amax_w complete
     float sc[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
@@ -614,33 +636,30 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       sc[m] = split_scale(a, &inv);
       if (tid == 0) scale_inv[m] = inv;
     }
-    // 2. x*s = hi + lo into xhl (row m: hi, row 8 + m: lo), 128-byte swizzled K-major layout; the
-    //    reloads hit L1.
-    for (int k0 = tid; k0 < nrows; k0 += 128 * kTcBatch) {
-      float v[M][kTcBatch];
+    // 2. x*s = hi + lo into xhl (row m: hi, row 8 + m: lo): one 16-byte chunk of 8 k values per row
+    //    and step, 128-byte swizzled K-major layout (chunk index ^ (row & 7)).
+    for (int k = tid * 8; k < kpad; k += 128 * 8) {
+      uint8_t* kblk = xhl + (k >> 6) * kTcXBlockBytes;
+      const int c16 = (k & 63) >> 3;
 #pragma unroll
-      for (int m = 0; m < M; ++m)
+      for (int m = 0; m < M; ++m) {
+        float v[8];
+        load8(xst + m * kpad + k, v);
+        uint32_t hp[4], lp[4];
 #pragma unroll
-        for (int u = 0; u < kTcBatch; ++u) {
-          const int k = k0 + u * 128;
-          v[m][u] = k < nrows ? to_f32(x[static_cast<size_t>(m) * args.K + kb + k]) : 0.f;
+        for (int j = 0; j < 4; ++j) {
+          const float a0 = v[2 * j] * sc[m], a1 = v[2 * j + 1] * sc[m];
+          const __half2 h = __floats2half2_rn(a0, a1);
+          const float2 hf = __half22float2(h);
+          const __half2 l = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+          hp[j] = *reinterpret_cast<const uint32_t*>(&h);
+          lp[j] = *reinterpret_cast<const uint32_t*>(&l);
         }
-#pragma unroll
-      for (int u = 0; u < kTcBatch; ++u) {
-        const int k = k0 + u * 128;
-        if (k < nrows) {
-          uint8_t* kbase = xhl + (k >> 6) * kTcXBlockBytes + ((k & 7) << 1);
-          const int kchunk16 = (k & 63) >> 3;
-#pragma unroll
-          for (int m = 0; m < M; ++m) {
-            const float xs = v[m][u] * sc[m];
-            const __half hi = __float2half_rn(xs);
-            const __half lo = __float2half_rn(xs - __half2float(hi));
-            const int rh = m, rl = 8 + m;
-            *reinterpret_cast<__half*>(kbase + (rh >> 3) * 1024 + (rh & 7) * 128 + ((kchunk16 ^ (rh & 7)) << 4)) = hi;
-            *reinterpret_cast<__half*>(kbase + (rl >> 3) * 1024 + (rl & 7) * 128 + ((kchunk16 ^ (rl & 7)) << 4)) = lo;
-          }
-        }
+        const int rh = m, rl = 8 + m;
+        *reinterpret_cast<uint4*>(kblk + (rh >> 3) * 1024 + (rh & 7) * 128 + ((c16 ^ (rh & 7)) << 4)) =
+            make_uint4(hp[0], hp[1], hp[2], hp[3]);
+        *reinterpret_cast<uint4*>(kblk + (rl >> 3) * 1024 + (rl & 7) * 128 + ((c16 ^ (rl & 7)) << 4)) =
+            make_uint4(lp[0], lp[1], lp[2], lp[3]);
       }
     }
     fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
@@ -705,17 +724,19 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   }
 }
 
-size_t skinny_tc_smem_bytes(int M, int kchunk) {
+size_t skinny_tc_smem_bytes(int M, int kchunk, int x_bytes) {
   const int nkb = (kchunk + 63) / 64;
   return 1024 + static_cast<size_t>(kTcStages) * kTcStageBytes + static_cast<size_t>(nkb) * kTcXBlockBytes +
-         static_cast<size_t>(M) * kTcStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
+         static_cast<size_t>(M) * nkb * 64 * x_bytes + static_cast<size_t>(M) * kTcStrip * 4 + 32 * 4 + 8 * 4 +
+         (2 * kTcStages + 2) * 8 + 8;
 }
 
 constexpr int kTcSmemAttrBytes = 1024 + kTcStages * kTcStageBytes + (kTcMaxChunk / 64) * kTcXBlockBytes +
-                                 8 * kTcStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
+                                 8 * kTcMaxChunk * 4 + 8 * kTcStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
+static_assert(kTcSmemAttrBytes <= 227 * 1024, "tensor-core skinny layout exceeds shared memory");
 
 // Column strips of kTcStrip; K split over up to 16 cluster ranks with chunks that are whole stages.
-SkinnyPlan plan_tc(int M, int K, int N, int ctas) {
+SkinnyPlan plan_tc(int M, int K, int N, int ctas, int x_bytes) {
   SkinnyPlan p{};
   p.strips = (N + kTcStrip - 1) / kTcStrip;
   int c = ctas / p.strips;
@@ -730,21 +751,22 @@ SkinnyPlan plan_tc(int M, int K, int N, int ctas) {
   p.csize = c;
   p.kchunk = kchunk;
   p.piece = kchunk;
-  p.smem_bytes = skinny_tc_smem_bytes(M, kchunk);
+  p.smem_bytes = skinny_tc_smem_bytes(M, kchunk, x_bytes);
   p.tc = kchunk <= kTcMaxChunk ? 1 : 0;
   return p;
 }
 
 // The largest cluster whose clusters are all resident at once (one CTA per SM with tensor memory).
 template <typename F>
-int plan_tc_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan* out) {
+int plan_tc_for(F* kern, int M, int K, int N, int x_bytes, const DeviceInfo& dev, SkinnyPlan* out) {
   static std::mutex mu;
   static std::unordered_map<uint64_t, SkinnyPlan> cache;
   int devid = 0;
   cudaError_t e = cudaGetDevice(&devid);
   if (e != cudaSuccess) return cuda_fail(e);
   const uint64_t key = (static_cast<uint64_t>(devid) << 58) ^ (static_cast<uint64_t>(M) << 54) ^
-                       (static_cast<uint64_t>(K) << 27) ^ static_cast<uint64_t>(N);
+                       (static_cast<uint64_t>(x_bytes) << 51) ^ (static_cast<uint64_t>(K) << 26) ^
+                       static_cast<uint64_t>(N);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -753,7 +775,7 @@ int plan_tc_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan*
       return G16_OK;
     }
   }
-  SkinnyPlan p = plan_tc(M, K, N, dev.sm_count);
+  SkinnyPlan p = plan_tc(M, K, N, dev.sm_count, x_bytes);
   int first = -1;
   while (p.tc) {
     cudaLaunchAttribute attr[1];
@@ -765,7 +787,7 @@ int plan_tc_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan*
     if (first < 0) first = active;
     p.active = active;
     if (active >= p.strips || p.csize == 1) break;
-    p = plan_tc(M, K, N, (p.csize - 1) * p.strips);
+    p = plan_tc(M, K, N, (p.csize - 1) * p.strips, x_bytes);
   }
   p.active_first = first;
   std::lock_guard<std::mutex> lk(mu);
@@ -782,10 +804,11 @@ int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void
   cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
   if (e != cudaSuccess) return cuda_fail(e);
   SkinnyPlan p;
-  int st = plan_tc_for(kern, M, K, N, dev, &p);
+  int st = plan_tc_for(kern, M, K, N, static_cast<int>(sizeof(TX)), dev, &p);
   if (st != G16_OK) return st;
   if (!p.tc) return launch_skinny_fma_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev);
-  if (p.smem_bytes != skinny_tc_smem_bytes(M, p.kchunk) || p.smem_bytes > static_cast<size_t>(kTcSmemAttrBytes))
+  if (p.smem_bytes != skinny_tc_smem_bytes(M, p.kchunk, static_cast<int>(sizeof(TX))) ||
+      p.smem_bytes > static_cast<size_t>(kTcSmemAttrBytes))
     return G16_ERR_ARG;
   CUtensorMap tmap;
   st = make_tmap_2d(&tmap, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
@@ -854,13 +877,13 @@ int skinny_plan_info(int M, int K, int N, int x_dtype, int* info, const DeviceIn
     auto kern = skinny_tc_kernel<1, float, false>;
     cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
     if (e != cudaSuccess) return cuda_fail(e);
-    st = plan_tc_for(kern, M, K, N, dev, &p);
+    st = plan_tc_for(kern, M, K, N, 4, dev, &p);
   } else {
     static std::atomic<uint64_t> attr_done{0};
     auto kern = skinny_tc_kernel<1, __half, false>;
     cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
     if (e != cudaSuccess) return cuda_fail(e);
-    st = plan_tc_for(kern, M, K, N, dev, &p);
+    st = plan_tc_for(kern, M, K, N, 2, dev, &p);
   }
   if (st != G16_OK) return st;
   info[0] = p.tc;
