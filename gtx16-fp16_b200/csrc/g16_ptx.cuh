@@ -87,6 +87,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// Bounded wait with cluster-scope acquire: for a barrier whose transactions are remote st.async
+// writes from other CTAs of the cluster. No abort short-cut: the caller must not leave while peers
+// may still write into its shared memory, so it waits out the (longer) limit instead.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// Named barriers for a subset of the CTA's warps (count = threads, a multiple of 32). bar.sync and
+// bar.arrive are the .aligned forms, which need the whole warp to execute them together, so the
+// warp is reconverged first. (The non-.aligned barrier.sync tolerates divergence but measured
+// several microseconds slower per use on sm_100a.)
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  __syncwarp();
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t count) {
+  __syncwarp();
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
 // ---------------------------------------------------------------------------------------------
@@ -241,6 +274,31 @@ __device__ __forceinline__ uint32_t cluster_nctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
+// Split phases of the same barrier: every thread of the cluster arrives once; a thread that waits
+// returns when all non-exited threads of the cluster have arrived.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+
+// Remote shared-memory stores that complete_tx on an mbarrier of the destination CTA
+// (both addresses from map_cluster onto the same rank).
+__device__ __forceinline__ void st_async_b32(uint32_t caddr, float v, uint32_t cbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(caddr),
+               "r"(__float_as_uint(v)), "r"(cbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v2(uint32_t caddr, float a, float b, uint32_t cbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(caddr),
+               "r"(__float_as_uint(a)), "r"(__float_as_uint(b)), "r"(cbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v4(uint32_t caddr, float a, float b, float c, float d, uint32_t cbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   caddr),
+               "r"(__float_as_uint(a)), "r"(__float_as_uint(b)), "r"(__float_as_uint(c)), "r"(__float_as_uint(d)),
+               "r"(cbar)
+               : "memory");
+}
+
 __device__ __forceinline__ uint32_t map_cluster(uint32_t saddr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
@@ -260,6 +318,16 @@ __device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t caddr) {
                : "r"(caddr)
                : "memory");
   return v;
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completing bytes on `bar` (no multicast).
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // Streaming 128-bit global load that does not allocate in L1 (weights are read exactly once).

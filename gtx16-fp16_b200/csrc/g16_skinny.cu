@@ -17,6 +17,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <unordered_map>
@@ -76,7 +77,7 @@ __device__ __forceinline__ void fma_row(float2 (&acc)[M][4], const uint4& wv, co
   }
 }
 
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
+__device__ __forceinline__ void consumer_sync() { named_bar_sync(1, kConsumers); }
 
 struct SkinnyArgs {
   const void* x;
@@ -84,6 +85,8 @@ struct SkinnyArgs {
   void* out;
   int* status;
   int K, N, kchunk, piece;
+  int stages;  // tensor-core variant: weight ring depth
+  int rows;    // tensor-core variant: weight rows per stage (32, 64 or 128)
 };
 
 // grid = (C, strips); cluster = (C, 1, 1); blockIdx.x is the CTA's rank in its cluster and selects
@@ -282,6 +285,8 @@ struct SkinnyPlan {
   int active_first = -1;  // resident clusters at the first cluster size tried
   int active = -1;        // resident clusters at the chosen cluster size
   int tc = 0;             // 1: tensor-core variant
+  int stages = 0;         // tensor-core variant: weight ring depth
+  int rows = 0;           // tensor-core variant: weight rows per stage
 };
 
 size_t skinny_smem_bytes(int M, int piece) {
@@ -430,26 +435,55 @@ int launch_skinny_fma_t(const void* x, const uint16_t* w, const float* bias, voi
 // tcgen05.mma kind::f16, M=128 (weight columns), N=16 (m' < 8: hi rows, m' >= 8: lo rows), K=16.
 // W is the MN-major A operand, streamed by TMA in 128-byte swizzled [32 rows x 64 columns] boxes
 // (the layout the GEMM uses for its B operand); xhl is a K-major B operand built in shared memory.
-// The partial for (m, n) is (D[n][m] + D[n][m+8]) / s; K chunks are then reduced across the
-// cluster in rank order as in the FMA variant. Work per 32-row stage is two MMAs whatever M is.
+// The partial for (m, n) is (D[n][m] + D[n][m+8]) / s. Work per 32-row stage is two MMAs whatever
+// M is.
+//
+// Reduction over the K chunks: rank r of the cluster finalises columns [r*slice, (r+1)*slice) of
+// the strip (slice = ceil(128 / csize)). Every rank pushes its partials for those columns into the
+// owner's shared memory with st.async, which completes bytes on the owner's mbarrier; the owner
+// sums the csize partials in rank order (deterministic) and stores. No cluster-wide barrier sits
+// on this path; one split arrive/wait pair at the start publishes the barriers' initialisation.
 //
 // A kernel that allocates tensor memory runs one CTA per SM, and a cluster must fit inside one
 // GPC, so strips are 128 columns wide (4096 columns -> 32 clusters of 4 CTAs on 148 SMs) rather
-// than the FMA variant's 256.
+// than the FMA variant's 256. Shared memory left over by x is all weight ring (up to 24 stages,
+// 192 KiB), and the producer fills the ring before the CTA-wide barrier, so the weight stream
+// starts while x is still being prepared.
 // =============================================================================================
 constexpr int kTcStrip = 128;                           // output columns per cluster (UMMA M)
-constexpr int kTcRows = 32;                             // weight rows per stage
-constexpr int kTcStages = 10;                           // 80 KiB of weights in flight per CTA
+constexpr int kTcMinRows = 32;                          // stage heights: 128, 64 or 32 weight rows
+constexpr int kTcMaxRows = 128;
+constexpr int kTcMaxStages = 24;                        // layout limit of the ring depth
 constexpr int kTcBoxCols = 64;                          // one 128-byte swizzle row of fp16
-constexpr int kTcBoxBytes = kTcRows * kTcBoxCols * 2;   // 4 KiB
-constexpr int kTcStageBytes = 2 * kTcBoxBytes;          // [32 rows x 128 columns] = 8 KiB
+__host__ __device__ constexpr int tc_box_bytes(int rows) { return rows * kTcBoxCols * 2; }  // [rows x 64]
+__host__ __device__ constexpr int tc_stage_bytes(int rows) { return 2 * tc_box_bytes(rows); }  // [rows x 128]
 constexpr int kTcThreads = 192;  // warps 0-3: x prep + epilogue, warp 4: TMEM + MMA, warp 5: TMA
 constexpr int kTcXRows = 16;     // UMMA N: x_hi rows 0..7, x_lo rows 8..15
-constexpr int kTcXBlockBytes = kTcXRows * 128;          // one 64-wide K block of xhl (2 KiB)
+// x_hi / x_lo, the K-major B operand (128-byte swizzle), per 64-wide K block of the chunk:
+//   M <= 4 ("packed"): one 8-row group [hi rows 0..M-1 | lo rows M..2M-1 | zero rows] (1 KiB); the
+//     operand's second 8-row group is a single shared 1 KiB zero block after the last K block,
+//     reached through a per-K-block stride-byte-offset (SBO) in the descriptor;
+//   M > 4: hi rows 0..7 then lo rows 8..15, zero rows past M (2 KiB).
+template <int M>
+struct XhlLayout {
+  static constexpr bool kPacked = M <= 4;
+  static constexpr int kBlockBytes = kPacked ? 1024 : 2048;
+  static constexpr int kLoRow = kPacked ? M : 8;  // first lo row = accumulator column of lo(x[0])
+};
+__host__ __device__ constexpr int tc_xhl_bytes(int M, int nkb) { return M <= 4 ? (nkb + 1) * 1024 : nkb * 2048; }
 constexpr int kTcMaxChunk = 2048;                       // xhl <= 64 KiB of shared memory
-constexpr uint32_t kTcTmemCols = 32;                    // one [128 x 16] fp32 accumulator (minimum allocation)
+constexpr int kTcRedBytes = (kTcStrip + kMaxCluster) * 8 * 4;  // pushed partials: csize x slice x MP fp32
+constexpr int kTcSmemLimit = 227 * 1024;
+// Consecutive 16-wide K steps go round-robin to kTcAcc independent [128 x 16] accumulators: a
+// dependent chain of N=16 MMAs into one accumulator runs at the MMA's latency (~0.1 us each),
+// far slower than the weight stream; independent ones overlap. Summed in fixed order at the end.
+constexpr int kTcAcc = 8;
+constexpr uint32_t kTcTmemCols = kTcAcc * kTcXRows;     // 128 columns (a power of two >= 32)
 
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_sync() { named_bar_sync(2, 128); }
+constexpr uint32_t kStartBar = 1;     // warp 5 arrives, warps 0-4 wait: start-up done
+constexpr uint32_t kTmemFreeBar = 3;  // warps 0-4: the epilogue has read the accumulator
+constexpr uint64_t kPushWaitLimitNs = 3ull * kWaitLimitNs;  // > any chain of waits before a peer pushes
 
 // Eight consecutive values from shared memory as fp32 (16-byte aligned source).
 __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
@@ -478,25 +512,38 @@ __device__ __forceinline__ float split_scale(float amax, float* inv) {
 template <int M, typename TX, bool OUT_F16>
 __global__ void __launch_bounds__(kTcThreads, 1)
 skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs args) {
+  constexpr int MP = MPad<M>::v;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* ring = smem;                                           // kTcStages x [2 boxes of 32 x 64]
+  const int S = args.stages;                                      // ring depth
+  const int R = args.rows;                                        // weight rows per stage
+  const int box_bytes = tc_box_bytes(R);
+  const int stage_bytes = tc_stage_bytes(R);
+  using XL = XhlLayout<M>;
+  uint8_t* ring = smem;                                           // S x [2 boxes of R x 64]
   const int nkb = (args.kchunk + 63) / 64;                        // 64-wide K blocks of x
-  uint8_t* xhl = ring + kTcStages * kTcStageBytes;                // nkb x 2 KiB, 1 KiB aligned
-  TX* xst = reinterpret_cast<TX*>(xhl + nkb * kTcXBlockBytes);    // [M][nkb * 64]: x chunk as loaded
-  float* part = reinterpret_cast<float*>(xst + M * nkb * 64);     // [M][kTcStrip]
-  float* amax_w = part + M * kTcStrip;                            // [4 warps][8]
+  const int kpad = nkb * 64;
+  // x as loaded, [M][kpad], overlays the ring's last stages: they are filled only after x_hi/x_lo
+  // are built (the producer issues stage 0 alone before then).
+  const int xst_stages = (M * kpad * static_cast<int>(sizeof(TX)) + stage_bytes - 1) / stage_bytes;
+  TX* xst = reinterpret_cast<TX*>(ring + (S - xst_stages) * stage_bytes);
+  uint8_t* xhl = ring + S * stage_bytes;                          // x_hi / x_lo, 1 KiB aligned
+  float* red = reinterpret_cast<float*>(xhl + tc_xhl_bytes(M, nkb));  // [csize][slice][MP]: pushed partials
+  float* amax_w = red + kTcRedBytes / 4;                          // [4 warps][8]
   float* scale_inv = amax_w + 32;                                 // [8]
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(scale_inv + 8);
-  uint64_t* empty_bar = full_bar + kTcStages;
-  uint64_t* xready_bar = empty_bar + kTcStages;
+  uint64_t* empty_bar = full_bar + kTcMaxStages;
+  uint64_t* xready_bar = empty_bar + kTcMaxStages;
   uint64_t* done_bar = xready_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  uint64_t* red_bar = done_bar + 1;
+  uint64_t* xfull_bar = red_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Self-check: the layout must end inside the launch's dynamic shared memory (uniform for the
   // grid, so every CTA returns before any barrier, TMEM allocation or shared-memory access).
-  if (static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) >
-      dynamic_smem_bytes()) {
+  if (S < 1 || S > kTcMaxStages || (R != 32 && R != 64 && R != 128) || xst_stages > S - 1 ||
+      static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) >
+          dynamic_smem_bytes()) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicExch(args.status, G16_ERR_ARG);
     return;
   }
@@ -510,56 +557,100 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   const int kb = rank * args.kchunk;
   const int ke = min(args.K, kb + args.kchunk);
   const int nrows = max(0, ke - kb);
-  const int nstages = (nrows + kTcRows - 1) / kTcRows;
+  const int nstages = (nrows + R - 1) / R;
+  const int slice = (kTcStrip + csize - 1) / csize;  // strip columns each rank finalises
+  const int own0 = rank * slice;
+  const int own_cnt = max(0, min(kTcStrip - own0, slice));
+  const int pre = min(S, nstages);                   // ring fill: stages issued without waiting
+  const TX* x = static_cast<const TX*>(args.x);
 
-  if (tid == 0) {
-    for (int st = 0; st < kTcStages; ++st) {
-      mbar_init(&full_bar[st], 1);
-      mbar_init(&empty_bar[st], 1);
-    }
-    mbar_init(xready_bar, 1);
-    mbar_init(done_bar, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 4) {
-    tmem_alloc(tmem_slot, kTcTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
+  // Start-up. The producer never waits on a CTA-wide barrier: TMA issue blocks while the TMA
+  // unit's queue is full, and a barrier behind it would hold back x and the tensor core.
+  // kStartBar (warp 5 arrives, warps 0-4 wait): barriers initialised, TMEM allocated. x is one
+  // bulk copy per row, issued right after barrier initialisation; the weight stream starts once x
+  // has landed (xfull_bar): issued together, x requests queue behind every CTA's share of the
+  // weights and the tensor core idles until they return. Only the first stage
+  // goes out before x_hi/x_lo are built (xready_bar): while a burst of TMA issues waits for the
+  // TMA unit, the shared-memory accesses of the x preparation stall behind it.
   if (warp == 5) {
+    if (lane == 0) {
+      for (int st = 0; st < S; ++st) {
+        mbar_init(&full_bar[st], 1);
+        mbar_init(&empty_bar[st], 1);
+      }
+      mbar_init(xready_bar, 1);
+      mbar_init(done_bar, 1);
+      mbar_init(red_bar, 1);
+      mbar_init(xfull_bar, 1);
+      *abort_flag = 0;
+      fence_barrier_init();  // cluster scope: peers push into red_bar after the cluster barrier
+      mbar_arrive_expect_tx(red_bar, static_cast<uint32_t>(csize * own_cnt * MP * 4));
+      // x chunk: one bulk copy per row (16-byte aligned: x is, K % 8 == 0 and kb % 32 == 0).
+      const uint32_t xrow_bytes = static_cast<uint32_t>(nrows * sizeof(TX));
+      mbar_arrive_expect_tx(xfull_bar, M * xrow_bytes);
+      if (xrow_bytes > 0) {
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+          bulk_load(xst + m * kpad, x + static_cast<size_t>(m) * args.K + kb, xrow_bytes, xfull_bar);
+      }
+    }
+    named_bar_arrive(kStartBar, 192);
+    cluster_arrive();  // every thread, once; the epilogue waits before its first remote store
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      tma_prefetch_desc(&tmap_w);
-      uint32_t phase = 0;
-      int stage = 0;
-      bool armed[kTcStages];
-      uint32_t armed_phase[kTcStages];
-      for (int st = 0; st < kTcStages; ++st) { armed[st] = false; armed_phase[st] = 0; }
-      bool ok = true;
-      for (int t = 0; t < nstages; ++t) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
-        uint8_t* dst = ring + stage * kTcStageBytes;
-        mbar_arrive_expect_tx(&full_bar[stage], kTcStageBytes);
-        armed[stage] = true;
-        armed_phase[stage] = phase;
+      bool ok = mbar_wait(xfull_bar, 0, abort_flag);
+      uint32_t armed = 0;        // stages holding an issued load
+      uint32_t armed_phase = 0;  // its phase parity, one bit per stage
+      // Fill the ring: never-used stages, no empty-barrier wait.
+      for (int t = 0; t < pre && ok; ++t) {
+        if (t == 1 && !mbar_wait(xready_bar, 0, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_bar[t], stage_bytes);
+        armed |= 1u << t;
 #pragma unroll
         for (int j = 0; j < kTcStrip / kTcBoxCols; ++j)
-          tma_load_2d(dst + j * kTcBoxBytes, &tmap_w, &full_bar[stage], n0 + j * kTcBoxCols, kb + t * kTcRows);
-        if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
+          tma_load_2d(ring + t * stage_bytes + j * box_bytes, &tmap_w, &full_bar[t], n0 + j * kTcBoxCols, kb + t * R);
+      }
+      int stage = pre;
+      uint32_t phase = 0;
+      if (stage == S) { stage = 0; phase = 1u; }
+      for (int t = pre; t < nstages && ok; ++t) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+        uint8_t* dst = ring + stage * stage_bytes;
+        mbar_arrive_expect_tx(&full_bar[stage], stage_bytes);
+        armed |= 1u << stage;
+        armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+#pragma unroll
+        for (int j = 0; j < kTcStrip / kTcBoxCols; ++j)
+          tma_load_2d(dst + j * box_bytes, &tmap_w, &full_bar[stage], n0 + j * kTcBoxCols, kb + t * R);
+        if (++stage == S) { stage = 0; phase ^= 1u; }
       }
       if (!ok) {
         *abort_flag = 1;
         atomicExch(args.status, G16_ERR_TIMEOUT);
-        for (int st = 0; st < kTcStages; ++st)
-          if (armed[st]) mbar_wait(&full_bar[st], armed_phase[st], nullptr);
+        for (int st = 0; st < S; ++st)
+          if ((armed >> st) & 1u) mbar_wait(&full_bar[st], (armed_phase >> st) & 1u, nullptr);
       }
     }
-  } else if (warp == 4) {
+    return;
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_relinquish();
+  } else {
+    // Zero the shared zero block of the packed layout while x is in flight.
+    if constexpr (XL::kPacked) {
+      if (tid < 64) reinterpret_cast<uint4*>(xhl + nkb * 1024)[tid] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  tc_fence_before();
+  named_bar_sync(kStartBar, 192);
+  tc_fence_after();
+  cluster_arrive();  // every thread, once; the epilogue waits before its first remote store
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 4) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       // D[n][m'] += W[k][n] * xhl[m'][k]: A = W (MN-major), B = xhl (K-major), M=128, N=16, K=16.
@@ -570,49 +661,47 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       for (int t = 0; t < nstages && ok; ++t) {
         if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sa = smem_u32(ring + stage * kTcStageBytes);
-#pragma unroll
-        for (int j = 0; j < kTcRows / kUmmaK; ++j) {
-          const int ks = t * (kTcRows / kUmmaK) + j;  // 16-wide K step within the chunk
-          // A: rows [16j, 16j + 16) of the stage: 2 KiB in; two 64-column boxes 4 KiB apart (LBO),
-          // 8-row k groups 1 KiB apart (SBO). B: K step ks of xhl.
-          const uint64_t adesc = smem_desc_sw128(sa + j * (kUmmaK * 128), kTcBoxBytes, 1024);
-          const uint64_t bdesc = smem_desc_sw128(smem_u32(xhl) + (ks >> 2) * kTcXBlockBytes + (ks & 3) * 32, 16, 1024);
-          umma_f16(tmem, adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
+        const uint32_t sa = smem_u32(ring + stage * stage_bytes);
+        for (int j = 0; j < R / kUmmaK; ++j) {
+          const int ks = t * (R / kUmmaK) + j;  // 16-wide K step within the chunk
+          // A: rows [16j, 16j + 16) of the stage: 2 KiB in; the two 64-column boxes are box_bytes
+          // apart (LBO), 8-row k groups 1 KiB apart (SBO).
+          const uint64_t adesc = smem_desc_sw128(sa + j * (kUmmaK * 128), box_bytes, 1024);
+          // B: K step ks of x_hi / x_lo; the second 8-row group is SBO bytes on (the zero block
+          // when packed).
+          const uint32_t sbo = XL::kPacked ? static_cast<uint32_t>(nkb - (ks >> 2)) * 1024u : 1024u;
+          const uint64_t bdesc =
+              smem_desc_sw128(smem_u32(xhl) + (ks >> 2) * XL::kBlockBytes + (ks & 3) * 32, 16, sbo);
+          umma_f16(tmem + static_cast<uint32_t>((ks % kTcAcc) * kTcXRows), adesc, bdesc, idesc,
+                   ks >= kTcAcc ? 1u : 0u);
         }
         umma_commit(&empty_bar[stage]);
-        if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
+        if (++stage == S) { stage = 0; phase ^= 1u; }
       }
       if (!ok) {
         *abort_flag = 1;
         atomicExch(args.status, G16_ERR_TIMEOUT);
       }
       umma_commit(done_bar);  // also the drain: arrives once every issued MMA has completed
-      mbar_wait(done_bar, 0, nullptr);  // TMEM is released below only after this
+      mbar_wait(done_bar, 0, nullptr);
     }
+    __syncwarp();
+    named_bar_sync(kTmemFreeBar, 160);  // the epilogue has read the accumulator
+    __syncwarp();                        // tcgen05.dealloc is .sync.aligned
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcTmemCols);
   } else {
     // ---------------- warps 0-3: build xhl, then the epilogue ----------------
-    const TX* x = static_cast<const TX*>(args.x);
-    // 0. copy this CTA's x chunk into xst (one memory latency; zero past the chunk) and zero xhl
-    //    (rows >= M, hi and lo, must contribute nothing).
-    const int kpad = nkb * 64;
-    constexpr int kVec = 16 / static_cast<int>(sizeof(TX));      // elements per 16-byte copy
-    for (int i = tid; i < M * (kpad / kVec); i += 128) {
-      const int m = i / (kpad / kVec);
-      const int k = (i - m * (kpad / kVec)) * kVec;
-      const int valid = min(kVec, max(0, nrows - k));
-      const TX* src = x + static_cast<size_t>(m) * args.K + kb + (valid > 0 ? k : 0);
-      cp_async_16(xst + m * kpad + k, src, static_cast<uint32_t>(valid * sizeof(TX)));
+    // xst rows hold [0, nrows) of the chunk; k >= nrows is masked below (nrows % 8 == 0).
+    if (!mbar_wait(xfull_bar, 0, abort_flag) && tid == 0) {
+      *abort_flag = 1;
+      atomicExch(args.status, G16_ERR_TIMEOUT);
     }
-    for (int i = tid; i < nkb * (kTcXBlockBytes / 16); i += 128)
-      reinterpret_cast<uint4*>(xhl)[i] = make_uint4(0u, 0u, 0u, 0u);
-    cp_async_wait_all();
-    epi_sync();
     // 1. per-row |max| over the chunk (8 values per 16 bytes read)
     float am[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) am[m] = 0.f;
-    for (int k = tid * 8; k < kpad; k += 128 * 8) {
+    for (int k = tid * 8; k < nrows; k += 128 * 8) {  // zeros past nrows do not change |max|
 #pragma unroll
       for (int m = 0; m < M; ++m) {
         float v[8];
@@ -636,15 +725,35 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       sc[m] = split_scale(a, &inv);
       if (tid == 0) scale_inv[m] = inv;
     }
-    // 2. x*s = hi + lo into xhl (row m: hi, row 8 + m: lo): one 16-byte chunk of 8 k values per row
-    //    and step, 128-byte swizzled K-major layout (chunk index ^ (row & 7)).
+    // 2. x*s = hi + lo into x_hi / x_lo (every row of the block written, zero rows included): one
+    //    16-byte chunk of 8 k values per row and step, 128-byte swizzled K-major layout (chunk
+    //    index ^ (row & 7)).
     for (int k = tid * 8; k < kpad; k += 128 * 8) {
-      uint8_t* kblk = xhl + (k >> 6) * kTcXBlockBytes;
+      uint8_t* kblk = xhl + (k >> 6) * XL::kBlockBytes;
       const int c16 = (k & 63) >> 3;
+      auto put = [&](int row, uint4 v) {
+        *reinterpret_cast<uint4*>(kblk + (row >> 3) * 1024 + (row & 7) * 128 + ((c16 ^ (row & 7)) << 4)) = v;
+      };
+      const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (XL::kPacked) {
+#pragma unroll
+        for (int row = 2 * M; row < 8; ++row) put(row, zero);
+      } else {
+#pragma unroll
+        for (int row = M; row < 8; ++row) {
+          put(row, zero);
+          put(8 + row, zero);
+        }
+      }
 #pragma unroll
       for (int m = 0; m < M; ++m) {
         float v[8];
-        load8(xst + m * kpad + k, v);
+        if (k < nrows) {
+          load8(xst + m * kpad + k, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = 0.f;
+        }
         uint32_t hp[4], lp[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -655,18 +764,16 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
           hp[j] = *reinterpret_cast<const uint32_t*>(&h);
           lp[j] = *reinterpret_cast<const uint32_t*>(&l);
         }
-        const int rh = m, rl = 8 + m;
-        *reinterpret_cast<uint4*>(kblk + (rh >> 3) * 1024 + (rh & 7) * 128 + ((c16 ^ (rh & 7)) << 4)) =
-            make_uint4(hp[0], hp[1], hp[2], hp[3]);
-        *reinterpret_cast<uint4*>(kblk + (rl >> 3) * 1024 + (rl & 7) * 128 + ((c16 ^ (rl & 7)) << 4)) =
-            make_uint4(lp[0], lp[1], lp[2], lp[3]);
+        put(m, make_uint4(hp[0], hp[1], hp[2], hp[3]));
+        put(XL::kLoRow + m, make_uint4(lp[0], lp[1], lp[2], lp[3]));
       }
     }
     fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
     epi_sync();
     if (tid == 0) mbar_arrive(xready_bar);
 
-    // 3. epilogue: wait for the last MMA, read the [128 x 16] accumulator (lane = weight column)
+    // 3. wait for the last MMA, read the kTcAcc [128 x 16] accumulators (lane = weight column)
+    //    and add those that were written, in accumulator order
     bool got = mbar_wait(done_bar, 0, abort_flag);
     got = __all_sync(0xffffffffu, got);
     if (!got && lane == 0) {
@@ -674,40 +781,62 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       atomicExch(args.status, G16_ERR_TIMEOUT);
     }
     tc_fence_after();
-    uint32_t d[16];
+    const int used = min(kTcAcc, nstages * (R / kUmmaK));
+    float acc16[kTcXRows];
+#pragma unroll
+    for (int i = 0; i < kTcXRows; ++i) acc16[i] = 0.f;
     __syncwarp();
-    tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(warp * 32) << 16), d);
-    tmem_ld_wait();
-    const int col = warp * 32 + lane;
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const float v = (nstages > 0 && got) ? (__uint_as_float(d[m]) + __uint_as_float(d[8 + m])) * scale_inv[m] : 0.f;
-      part[m * kTcStrip + col] = v;
+    for (int q = 0; q < kTcAcc / 2; ++q) {
+      uint32_t d[32];
+      __syncwarp();  // tcgen05.ld is .sync.aligned
+      tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(q * 32), d);
+      tmem_ld_wait();
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        if (2 * q + h < used) {
+#pragma unroll
+          for (int i = 0; i < kTcXRows; ++i) acc16[i] += __uint_as_float(d[h * kTcXRows + i]);
+        }
     }
-  }
+    tc_fence_before();
+    named_bar_arrive(kTmemFreeBar, 160);
+    const bool live = nstages > 0 && got;
+    float v[MP];
+#pragma unroll
+    for (int m = 0; m < MP; ++m)
+      v[m] = (m < M && live) ? (acc16[m] + acc16[XL::kLoRow + m]) * scale_inv[m] : 0.f;
 
-  // Reduce across the cluster in rank order; CTA `rank` finalises a contiguous share of outputs.
-  tc_fence_before();
-  cluster_sync();
-  tc_fence_after();
-  if (warp < 4) {
-    const int total = M * kTcStrip;
-    const int share = (total + csize - 1) / csize;
-    const int i0 = rank * share;
-    const int i1 = min(total, i0 + share);
-    const uint32_t part_addr = smem_u32(part);
-    for (int i = i0 + tid; i < i1; i += 128) {
-      const int m = i / kTcStrip, c = i - m * kTcStrip;
-      const int n = n0 + c;
+    // 4. push column `tid` to the rank that owns it (every path pushes: owners wait for all bytes)
+    const int owner = tid / slice;
+    const int j = tid - owner * slice;
+    cluster_wait();  // peers' barriers are initialised
+    const uint32_t dst = map_cluster(smem_u32(red + (rank * slice + j) * MP), static_cast<uint32_t>(owner));
+    const uint32_t rbar = map_cluster(smem_u32(red_bar), static_cast<uint32_t>(owner));
+    if constexpr (MP == 1) {
+      st_async_b32(dst, v[0], rbar);
+    } else if constexpr (MP == 2) {
+      st_async_v2(dst, v[0], v[1], rbar);
+    } else {
+#pragma unroll
+      for (int q = 0; q < MP / 4; ++q)
+        st_async_v4(dst + 16u * q, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3], rbar);
+    }
+
+    // 5. finalise the owned columns: sum the csize partials in rank order, add bias, store
+    if (!mbar_wait_cluster(red_bar, 0, kPushWaitLimitNs)) {
+      if (tid == 0) {
+        *abort_flag = 1;
+        atomicExch(args.status, G16_ERR_TIMEOUT);
+      }
+      return;
+    }
+    for (int i = tid; i < M * own_cnt; i += 128) {
+      const int m = i / own_cnt, jj = i - m * own_cnt;
+      const int n = n0 + own0 + jj;
       if (n < args.N) {
-        float pv[kMaxCluster];
-#pragma unroll
-        for (int q = 0; q < kMaxCluster; ++q)
-          pv[q] = q < csize ? ld_cluster_f32(map_cluster(part_addr + 4u * i, q)) : 0.f;
         float acc = 0.f;
-#pragma unroll
-        for (int q = 0; q < kMaxCluster; ++q)
-          if (q < csize) acc += pv[q];
+        for (int q = 0; q < csize; ++q) acc += red[(q * slice + jj) * MP + m];
         if (args.bias != nullptr) acc += args.bias[n];
         if constexpr (OUT_F16) {
           reinterpret_cast<__half*>(args.out)[static_cast<size_t>(m) * args.N + n] = __float2half_rn(acc);
@@ -717,43 +846,76 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       }
     }
   }
-  cluster_sync();  // keep `part` alive until every peer has read it
-  if (warp == 4) {
-    __syncwarp();
-    tmem_dealloc(tmem, kTcTmemCols);
-  }
 }
 
-size_t skinny_tc_smem_bytes(int M, int kchunk, int x_bytes) {
+// Ring stages that x (as loaded) overlays.
+int tc_xst_stages(int M, int kchunk, int x_bytes, int rows) {
+  const int kpad = (kchunk + 63) / 64 * 64;
+  return (M * kpad * x_bytes + tc_stage_bytes(rows) - 1) / tc_stage_bytes(rows);
+}
+
+size_t skinny_tc_smem_bytes(int M, int kchunk, int rows, int stages) {
   const int nkb = (kchunk + 63) / 64;
-  return 1024 + static_cast<size_t>(kTcStages) * kTcStageBytes + static_cast<size_t>(nkb) * kTcXBlockBytes +
-         static_cast<size_t>(M) * nkb * 64 * x_bytes + static_cast<size_t>(M) * kTcStrip * 4 + 32 * 4 + 8 * 4 +
-         (2 * kTcStages + 2) * 8 + 8;
+  return 1024 + static_cast<size_t>(stages) * tc_stage_bytes(rows) + tc_xhl_bytes(M, nkb) + kTcRedBytes + 32 * 4 +
+         8 * 4 + (2 * kTcMaxStages + 4) * 8 + 8;
 }
 
-constexpr int kTcSmemAttrBytes = 1024 + kTcStages * kTcStageBytes + (kTcMaxChunk / 64) * kTcXBlockBytes +
-                                 8 * kTcMaxChunk * 4 + 8 * kTcStrip * 4 + 32 * 4 + 8 * 4 + (2 * kTcStages + 2) * 8 + 8;
-static_assert(kTcSmemAttrBytes <= 227 * 1024, "tensor-core skinny layout exceeds shared memory");
+// The largest layout (8 fp32 rows, the longest chunk, 128-row stages) must still hold x in the
+// ring's last stages and leave one stage before them.
+static_assert(1024 + 3 * tc_stage_bytes(kTcMaxRows) + tc_xhl_bytes(8, kTcMaxChunk / 64) + kTcRedBytes + 32 * 4 +
+                      8 * 4 + (2 * kTcMaxStages + 4) * 8 + 8 <=
+                  kTcSmemLimit &&
+                  8 * kTcMaxChunk * 4 <= 2 * tc_stage_bytes(kTcMaxRows),
+              "tensor-core skinny layout exceeds shared memory");
+static_assert(kTcMaxStages <= 32, "armed-stage bit masks are 32 bits wide");
 
-// Column strips of kTcStrip; K split over up to 16 cluster ranks with chunks that are whole stages.
-SkinnyPlan plan_tc(int M, int K, int N, int ctas, int x_bytes) {
+// Column strips of kTcStrip; K split over up to 16 cluster ranks with chunks that are whole
+// stages of `rows` weight rows, at least two stages per rank.
+SkinnyPlan plan_tc_rows(int M, int K, int N, int ctas, int x_bytes, int rows) {
   SkinnyPlan p{};
   p.strips = (N + kTcStrip - 1) / kTcStrip;
   int c = ctas / p.strips;
   if (c < 1) c = 1;
   if (c > kMaxCluster) c = kMaxCluster;
-  const int max_by_k = K / (2 * kTcRows) > 0 ? K / (2 * kTcRows) : 1;
+  const int max_by_k = K / (2 * rows) > 0 ? K / (2 * rows) : 1;
   if (c > max_by_k) c = max_by_k;
   int kchunk = (K + c - 1) / c;
-  kchunk = (kchunk + kTcRows - 1) / kTcRows * kTcRows;
+  kchunk = (kchunk + rows - 1) / rows * rows;
   c = (K + kchunk - 1) / kchunk;
   if (c < 1) c = 1;
   p.csize = c;
   p.kchunk = kchunk;
   p.piece = kchunk;
-  p.smem_bytes = skinny_tc_smem_bytes(M, kchunk, x_bytes);
-  p.tc = kchunk <= kTcMaxChunk ? 1 : 0;
+  p.rows = rows;
+  // Ring depth: measured on B200 (4096 x 4096), 3 stages of 128 rows beat 2, 4, 5 and 6: the
+  // bandwidth is there with 96 KiB in flight per CTA, and deeper rings queue more TMA issues in
+  // front of the MMA issues. x as loaded overlays the last stages, so at least one precedes them.
+  const size_t fixed = skinny_tc_smem_bytes(M, kchunk, rows, 0);
+  int stages = fixed < static_cast<size_t>(kTcSmemLimit)
+                   ? static_cast<int>((static_cast<size_t>(kTcSmemLimit) - fixed) / tc_stage_bytes(rows))
+                   : 0;
+  const int xst_stages = tc_xst_stages(M, kchunk, x_bytes, rows);
+  const int preferred = rows == 128 ? 3 : rows == 64 ? 4 : 8;
+  stages = std::min(stages, kTcMaxStages);
+  stages = std::min(stages, std::max(std::min(preferred, kchunk / rows), xst_stages + 1));
+  p.stages = stages;
+  p.smem_bytes = skinny_tc_smem_bytes(M, kchunk, rows, stages);
+  p.tc = (kchunk <= kTcMaxChunk && stages >= 2 && stages >= xst_stages + 1) ? 1 : 0;
   return p;
+}
+
+// Each stage costs the MMA issuer a commit and a barrier round trip whatever its height, so the
+// tallest stage wins unless a shorter one puts more CTAs to work.
+SkinnyPlan plan_tc(int M, int K, int N, int ctas, int x_bytes) {
+  SkinnyPlan best = plan_tc_rows(M, K, N, ctas, x_bytes, kTcMinRows);
+  for (int rows = kTcMaxRows; rows > kTcMinRows; rows /= 2) {
+    const SkinnyPlan p = plan_tc_rows(M, K, N, ctas, x_bytes, rows);
+    if (p.tc && (!best.tc || p.csize >= best.csize)) {
+      best = p;
+      break;
+    }
+  }
+  return best;
 }
 
 // The largest cluster whose clusters are all resident at once (one CTA per SM with tensor memory).
@@ -801,18 +963,20 @@ int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void
                        const DeviceInfo& dev) {
   static std::atomic<uint64_t> attr_done{0};
   auto kern = skinny_tc_kernel<M, TX, OUT_F16>;
-  cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
+  cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemLimit);
   if (e != cudaSuccess) return cuda_fail(e);
   SkinnyPlan p;
   int st = plan_tc_for(kern, M, K, N, static_cast<int>(sizeof(TX)), dev, &p);
   if (st != G16_OK) return st;
   if (!p.tc) return launch_skinny_fma_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev);
-  if (p.smem_bytes != skinny_tc_smem_bytes(M, p.kchunk, static_cast<int>(sizeof(TX))) ||
-      p.smem_bytes > static_cast<size_t>(kTcSmemAttrBytes))
+  if (p.stages < 2 || p.stages > kTcMaxStages ||
+      p.smem_bytes != skinny_tc_smem_bytes(M, p.kchunk, p.rows, p.stages) ||
+      p.stages < tc_xst_stages(M, p.kchunk, static_cast<int>(sizeof(TX)), p.rows) + 1 ||
+      p.smem_bytes > static_cast<size_t>(kTcSmemLimit))
     return G16_ERR_ARG;
   CUtensorMap tmap;
   st = make_tmap_2d(&tmap, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
-                    kTcRows, kTcBoxCols, CU_TENSOR_MAP_SWIZZLE_128B);
+                    p.rows, kTcBoxCols, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
   SkinnyArgs a{};
   a.x = x;
@@ -824,6 +988,8 @@ int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void
   a.N = N;
   a.kchunk = p.kchunk;
   a.piece = p.kchunk;
+  a.stages = p.stages;
+  a.rows = p.rows;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(p, s, attr);
   cfg.blockDim = dim3(kTcThreads, 1, 1);
@@ -875,13 +1041,13 @@ int skinny_plan_info(int M, int K, int N, int x_dtype, int* info, const DeviceIn
   if (x_dtype == G16_F32) {
     static std::atomic<uint64_t> attr_done{0};
     auto kern = skinny_tc_kernel<1, float, false>;
-    cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
+    cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemLimit);
     if (e != cudaSuccess) return cuda_fail(e);
     st = plan_tc_for(kern, M, K, N, 4, dev, &p);
   } else {
     static std::atomic<uint64_t> attr_done{0};
     auto kern = skinny_tc_kernel<1, __half, false>;
-    cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemAttrBytes);
+    cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemLimit);
     if (e != cudaSuccess) return cuda_fail(e);
     st = plan_tc_for(kern, M, K, N, 2, dev, &p);
   }
