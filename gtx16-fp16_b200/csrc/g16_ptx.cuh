@@ -120,6 +120,15 @@ __device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t count) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch. launch_dependents lets the next kernel of the stream (launched
+// with programmatic stream serialization) start its on-chip set-up early; grid_dependency_wait
+// returns once the preceding kernel has completed and its memory is visible (at once when the
+// launch had no programmatic dependency). Global memory is touched only after the wait.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
 // ---------------------------------------------------------------------------------------------

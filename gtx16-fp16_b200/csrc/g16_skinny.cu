@@ -544,7 +544,10 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   if (S < 1 || S > kTcMaxStages || (R != 32 && R != 64 && R != 128) || xst_stages > S - 1 ||
       static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) >
           dynamic_smem_bytes()) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicExch(args.status, G16_ERR_ARG);
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {
+      grid_dependency_wait();
+      atomicExch(args.status, G16_ERR_ARG);
+    }
     return;
   }
 
@@ -558,6 +561,9 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
   const int ke = min(args.K, kb + args.kchunk);
   const int nrows = max(0, ke - kb);
   const int nstages = (nrows + R - 1) / R;
+  // The next kernel may start its set-up on free SMs now; it reads nothing this one writes before
+  // its own grid_dependency_wait.
+  if (tid == 0) grid_launch_dependents();
   const int slice = (kTcStrip + csize - 1) / csize;  // strip columns each rank finalises
   const int own0 = rank * slice;
   const int own_cnt = max(0, min(kTcStrip - own0, slice));
@@ -585,6 +591,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       *abort_flag = 0;
       fence_barrier_init();  // cluster scope: peers push into red_bar after the cluster barrier
       mbar_arrive_expect_tx(red_bar, static_cast<uint32_t>(csize * own_cnt * MP * 4));
+      grid_dependency_wait();  // x, W: written by the preceding kernel, possibly
       // x chunk: one bulk copy per row (16-byte aligned: x is, K % 8 == 0 and kb % 32 == 0).
       const uint32_t xrow_bytes = static_cast<uint32_t>(nrows * sizeof(TX));
       mbar_arrive_expect_tx(xfull_bar, M * xrow_bytes);
@@ -645,6 +652,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
       if (tid < 64) reinterpret_cast<uint4*>(xhl + nkb * 1024)[tid] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
+  grid_dependency_wait();  // bias, out, status
   tc_fence_before();
   named_bar_sync(kStartBar, 192);
   tc_fence_after();
@@ -990,9 +998,14 @@ int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void
   a.piece = p.kchunk;
   a.stages = p.stages;
   a.rows = p.rows;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = make_cfg(p, s, attr);
   cfg.blockDim = dim3(kTcThreads, 1, 1);
+  // Programmatic dependent launch: back-to-back calls overlap one launch's set-up with the
+  // previous one's tail (the kernel waits for its predecessor before any global access).
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, tmap, a);
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();
