@@ -264,6 +264,67 @@ int g16_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype,
                      static_cast<cudaStream_t>(stream), *dev);
 }
 
+int g16_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
+                     const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
+                     void* stream) {
+  if (dst == nullptr || ndst < 1 || ndst > G16_SCATTER_MAX_DST) return G16_ERR_ARG;
+  if (M < 0 || K <= 0 || N < 0 || col0 < 0 || ldc < static_cast<long long>(col0) + N) return G16_ERR_ARG;
+  if (out_dtype != G16_F32 && out_dtype != G16_F16) return G16_ERR_ARG;
+  if (K % 8 != 0 || N % 8 != 0 || col0 % 8 != 0 || ldc % 8 != 0) return G16_ERR_UNSUPPORTED;
+  if (M == 0 || N == 0) return G16_OK;
+  if (a16 == nullptr || b16 == nullptr) return G16_ERR_ARG;
+  if (!aligned16(a16) || !aligned16(b16) || (bias != nullptr && !aligned16(bias))) return G16_ERR_ALIGN;
+  for (int d = 0; d < ndst; ++d) {
+    if (dst[d] == nullptr) return G16_ERR_ARG;
+    if (!aligned16(dst[d])) return G16_ERR_ALIGN;
+  }
+  int st = G16_OK;
+  const DeviceInfo* dev = device_info(&st);
+  if (dev == nullptr) return st;
+  return launch_gemm_scatter(a16, b16, dst, ndst, out_dtype, bias, rscale, M, K, N, ldc, col0,
+                             static_cast<cudaStream_t>(stream), *dev);
+}
+
+int g16_ipc_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return G16_ERR_ARG;
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return cuda_fail(e);
+  return G16_OK;
+}
+
+int g16_ipc_free(void* ptr) {
+  if (ptr == nullptr) return G16_ERR_ARG;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? G16_OK : cuda_fail(e);
+}
+
+int g16_ipc_get_handle(void* ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == G16_IPC_HANDLE_BYTES, "IPC handle size");
+  if (ptr == nullptr || handle == nullptr) return G16_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return cuda_fail(e);
+  std::memcpy(handle, &h, sizeof(h));
+  return G16_OK;
+}
+
+int g16_ipc_open(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return G16_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e);
+  return G16_OK;
+}
+
+int g16_ipc_close(void* ptr) {
+  if (ptr == nullptr) return G16_ERR_ARG;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? G16_OK : cuda_fail(e);
+}
+
 int g16_skinny_plan(int M, int K, int N, int x_dtype, int* info) {
   if (info == nullptr || K <= 0 || N <= 0 || (x_dtype != G16_F32 && x_dtype != G16_F16)) return G16_ERR_ARG;
   int st = G16_OK;

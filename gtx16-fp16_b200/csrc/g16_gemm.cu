@@ -44,9 +44,18 @@ constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemCols = 2 * kBN;         // double-buffered accumulator
 constexpr int kGroupM = 8;                      // tile rasterisation: 8 tile-rows per group
 constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers etc.*/;
+// Scatter epilogue: each epilogue warp transposes its 32 rows x 128 bytes through shared memory so
+// that every store instruction writes whole 128-byte row segments (8 lanes per row).
+constexpr int kMaxDst = 8;
+constexpr uint32_t kEpiStageBytes = (kEpiThreads / 32) * 32 * 128;  // 16 KiB
+constexpr size_t kSmemBytesScatter = kSmemBytes + kEpiStageBytes;
 
 struct GemmArgs {
   void* out;
+  void* dst[kMaxDst];  // scatter: destination buffers, each [M, ldc]; the tile lands at column col0 + n
+  int ndst;
+  long long ldc;
+  int col0;
   const float* bias;
   const float* rscale;
   float* partials;  // [m_tiles * n_tiles][ksplit][kBM][kBN] fp32 (split-K only), tile = mt * n_tiles + nt
@@ -116,7 +125,29 @@ __device__ __forceinline__ void store_row32(const GemmArgs& a, int row, int col0
   }
 }
 
+// One 128-byte row segment per lane-octet: the scatter epilogue's coalesced store of a warp's
+// staged [32 rows x 128 bytes] (16-byte chunk j of row r sits at chunk j ^ (r & 7)).
 template <bool OUT_F16>
+__device__ __forceinline__ void scatter_rows(const GemmArgs& a, const uint8_t* stage, int row0, int col_first,
+                                             int lane) {
+  constexpr int kElem = OUT_F16 ? 2 : 4;
+  constexpr int kPerChunk = 16 / kElem;  // elements per 16-byte chunk
+  const int c = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {  // 4 rows (8 lanes each) per instruction
+    const int r = i * 4 + (lane >> 3);
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 128 + ((c ^ (r & 7)) << 4));
+    const int row = row0 + r;
+    const int col = col_first + c * kPerChunk;  // local column
+    if (row < a.M && col < a.N) {                // N % 8 == 0: whole chunks are in or out
+      const long long off = (static_cast<long long>(row) * a.ldc + a.col0 + col) * kElem;
+      for (int d = 0; d < a.ndst; ++d)
+        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.dst[d]) + off) = v;
+    }
+  }
+}
+
+template <bool OUT_F16, bool SCATTER>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
             const GemmArgs args) {
@@ -126,7 +157,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   // every access into a generic-address load).
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* stage_base = smem;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint8_t* epi_stage = smem + kStages * kStageBytes;  // scatter only: kEpiStageBytes
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_stage + (SCATTER ? kEpiStageBytes : 0));
   uint64_t* empty_bar = full_bar + kStages;
   uint64_t* tfull_bar = empty_bar + kStages;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -259,7 +291,63 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       if (!got && lane == 0) report_timeout(args.status, abort_flag);
       const int row = w.mt * kBM + r_local;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
-      if (args.ksplit == 1) {
+      if constexpr (SCATTER) {
+        // ksplit == 1 (enforced by the launcher). 128 bytes per row per pass: 64 fp16 or 32 fp32
+        // columns; every destination gets each row segment once.
+        if (!got) break;
+        tc_fence_after();
+        const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
+        constexpr int kCols = OUT_F16 ? 64 : 32;
+        uint8_t* my_stage = epi_stage + quarter * (32 * 128);
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN; c0 += kCols) {
+          const int gcol = w.nt * kBN + c0;  // local column of the pass
+          uint4 packed[8];
+#pragma unroll
+          for (int h = 0; h < kCols / 32; ++h) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(t_row + c0 + h * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int col = gcol + h * 32 + 8 * g;
+              float o[8];
+              if (args.bias != nullptr && col < args.N) {
+                const float4 b0 = __ldg(reinterpret_cast<const float4*>(args.bias + col));
+                const float4 b1 = __ldg(reinterpret_cast<const float4*>(args.bias + col + 4));
+                const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[j] = fmaf(__uint_as_float(r[8 * g + j]), rs, bb[j]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[j] = __uint_as_float(r[8 * g + j]) * rs;
+              }
+              if constexpr (OUT_F16) {
+                __half2 hh[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) hh[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+                packed[h * 4 + g] = *reinterpret_cast<const uint4*>(hh);
+              } else {
+                packed[h * 8 + 2 * g] = make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]),
+                                                   __float_as_uint(o[2]), __float_as_uint(o[3]));
+                packed[h * 8 + 2 * g + 1] = make_uint4(__float_as_uint(o[4]), __float_as_uint(o[5]),
+                                                       __float_as_uint(o[6]), __float_as_uint(o[7]));
+              }
+            }
+          }
+          // this lane's row: 8 chunks of 16 bytes, swizzled by row
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(my_stage + lane * 128 + ((j ^ (lane & 7)) << 4)) = packed[j];
+          __syncwarp();
+          scatter_rows<OUT_F16>(args, my_stage, w.mt * kBM + quarter * 32, gcol, lane);
+          __syncwarp();  // the stage is rewritten by the next pass
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      } else if (args.ksplit == 1) {
         if (!got) break;
         tc_fence_after();
         const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
@@ -303,6 +391,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
   }
 
+  // Scatter: stores into peer memory (NVLink) are made visible system-wide before the grid ends.
+  if constexpr (SCATTER) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -405,7 +495,7 @@ cudaError_t ensure_smem_attr(F* kern, std::atomic<uint64_t>& done, int bytes) {
   return e;
 }
 
-std::atomic<uint64_t> g_attr_f16{0}, g_attr_f32{0};
+std::atomic<uint64_t> g_attr_f16{0}, g_attr_f32{0}, g_attr_sc16{0}, g_attr_sc32{0};
 
 template <bool OUT_F16>
 cudaError_t launch_reduce(const GemmArgs& args, cudaStream_t s, const DeviceInfo& dev) {
@@ -471,13 +561,13 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
   const int grid = args.units < dev.sm_count ? args.units : dev.sm_count;
   cudaError_t e;
   if (out_dtype == G16_F16) {
-    e = ensure_smem_attr(gemm_kernel<true>, g_attr_f16, static_cast<int>(kSmemBytes));
+    e = ensure_smem_attr(gemm_kernel<true, false>, g_attr_f16, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return cuda_fail(e);
-    gemm_kernel<true><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
+    gemm_kernel<true, false><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
   } else {
-    e = ensure_smem_attr(gemm_kernel<false>, g_attr_f32, static_cast<int>(kSmemBytes));
+    e = ensure_smem_attr(gemm_kernel<false, false>, g_attr_f32, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return cuda_fail(e);
-    gemm_kernel<false><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
+    gemm_kernel<false, false><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
@@ -487,6 +577,58 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
     if (e != cudaSuccess) return cuda_fail(e);
     note_launch();
   }
+  return G16_OK;
+}
+
+int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
+                        const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
+                        cudaStream_t s, const DeviceInfo& dev) {
+  if (ndst < 1 || ndst > kMaxDst) return G16_ERR_ARG;
+  if (M <= 0 || N <= 0) return G16_OK;
+  GemmArgs args{};
+  for (int d = 0; d < ndst; ++d) {
+    if (dst[d] == nullptr) return G16_ERR_ARG;
+    args.dst[d] = dst[d];
+  }
+  args.ndst = ndst;
+  args.ldc = ldc;
+  args.col0 = col0;
+  args.bias = bias;
+  args.rscale = rscale;
+  args.status = device_status_ptr();
+  if (args.status == nullptr) return G16_ERR_CUDA;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.m_tiles = (M + kBM - 1) / kBM;
+  args.n_tiles = (N + kBN - 1) / kBN;
+  args.tiles = args.m_tiles * args.n_tiles;
+  args.kblocks = (K + kBK - 1) / kBK;
+  args.kb_per_split = args.kblocks;
+  args.ksplit = 1;
+  args.units = args.tiles;
+
+  CUtensorMap ta, tb;
+  int st = make_tmap_2d(&ta, a16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(M),
+                        static_cast<uint64_t>(K), kBM, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != G16_OK) return st;
+  st = make_tmap_2d(&tb, b16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                    kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != G16_OK) return st;
+  const int grid = args.units < dev.sm_count ? args.units : dev.sm_count;
+  cudaError_t e;
+  if (out_dtype == G16_F16) {
+    e = ensure_smem_attr(gemm_kernel<true, true>, g_attr_sc16, static_cast<int>(kSmemBytesScatter));
+    if (e != cudaSuccess) return cuda_fail(e);
+    gemm_kernel<true, true><<<grid, kThreads, kSmemBytesScatter, s>>>(ta, tb, args);
+  } else {
+    e = ensure_smem_attr(gemm_kernel<false, true>, g_attr_sc32, static_cast<int>(kSmemBytesScatter));
+    if (e != cudaSuccess) return cuda_fail(e);
+    gemm_kernel<false, true><<<grid, kThreads, kSmemBytesScatter, s>>>(ta, tb, args);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  note_launch();
   return G16_OK;
 }
 

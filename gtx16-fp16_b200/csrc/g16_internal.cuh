@@ -45,6 +45,10 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
                 const float* rscale, int M, int K, int N, int ksplit, void* ws, size_t ws_bytes, cudaStream_t s,
                 const DeviceInfo& dev);
 size_t gemm_workspace_bytes(int M, int K, int N, int ksplit);
+// Sharded GEMM whose fp16/fp32 output tiles go to ndst buffers [M, ldc] at column col0 (no split-K).
+int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
+                        const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
+                        cudaStream_t s, const DeviceInfo& dev);
 int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
 
 // 2-D TMA tensor map over a row-major [rows, cols] matrix with a [box_rows, box_cols] box (g16_tmap.cu).

@@ -25,6 +25,8 @@ _lock = threading.Lock()
 
 # Every exported symbol of include/g16.h with its ctypes signature (restype, argtypes).
 _P, _I, _F, _Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+IPC_HANDLE_BYTES = 64       # G16_IPC_HANDLE_BYTES
+SCATTER_MAX_DST = 8         # G16_SCATTER_MAX_DST
 SIGNATURES = {
     "g16_mm_t": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "g16_mm_t_workspace_bytes": (_Z, [_I, _I, _I, _I]),
@@ -34,6 +36,12 @@ SIGNATURES = {
     "g16_gemm_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g16_gemm_auto_ksplit": (_I, [_I, _I, _I]),
     "g16_gemm_static_scratch": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P]),
+    "g16_gemm_scatter": (_I, [_P, _P, ctypes.POINTER(_P), _I, _I, _P, _P, _I, _I, _I, ctypes.c_longlong, _I, _P]),
+    "g16_ipc_alloc": (_I, [_Z, ctypes.POINTER(_P)]),
+    "g16_ipc_free": (_I, [_P]),
+    "g16_ipc_get_handle": (_I, [_P, _P]),
+    "g16_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "g16_ipc_close": (_I, [_P]),
     "g16_skinny_plan": (_I, [_I, _I, _I, _I, ctypes.POINTER(_I)]),
     "g16_device_status": (_I, [ctypes.POINTER(_I), _I, _P]),
     "g16_launch_count": (ctypes.c_uint64, []),

@@ -4,16 +4,21 @@ The reference is single-GPU. Two ways of using several GPUs of one box are provi
 shapes that shard naturally:
 
 * ``ShardedMatmul``: out[M, N] = a[M, K] @ w_t[K, N] with w_t split by columns. Rank r keeps its
-  column shard w_t[:, n_r0:n_r1] resident, computes out[:, n_r0:n_r1] with ``mm_t`` and the shards
-  are exchanged with one NCCL all-gather (the only collective on the path). Every rank ends with
-  the full output. Shard boundaries are multiples of 8 columns (the kernels' N % 8 rule).
+  column shard w_t[:, n_r0:n_r1] resident and computes out[:, n_r0:n_r1]. On CUDA with NCCL and
+  fp16 activations the exchange is fused into the GEMM: the epilogue stores every output tile
+  into each rank's full output buffer (``PeerBuffer``: CUDA IPC mappings over NVLink), so the
+  all-gather overlaps the math and no separate copy pass is needed; two one-element all-reduces
+  per call order the buffers' reuse. Otherwise (fp32 activations, M <= 8, gloo) the shards are
+  computed with ``mm_t`` and exchanged with one NCCL all-gather. Every rank ends with the full
+  output. Shard boundaries are multiples of 8 columns (the kernels' N % 8 rule).
 * ``batch_slice``: data parallelism over a batch of independent inputs (model inference): rank r
   takes a contiguous slice; there is no collective on the data path, only an optional gather of
   the (small) results.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
+import ctypes
+from dataclasses import dataclass, field
 
 import torch
 import torch.distributed as dist
@@ -41,6 +46,68 @@ def batch_slice(batch: int, world: int, rank: int) -> slice:
     return slice(b0, b0 + base + (1 if rank < extra else 0))
 
 
+class _CudaArray:
+    """A raw device allocation described by __cuda_array_interface__ (wrapped by torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape: tuple, dtype: torch.dtype):
+        typestr = {torch.float16: "<f2", torch.float32: "<f4"}[dtype]
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerBuffer:
+    """A [rows, cols] buffer on every rank of `group`, mapped into every other rank with CUDA IPC.
+
+    ``tensor`` is this rank's buffer; ``ptrs[r]`` is rank r's buffer as this process addresses it
+    (its own for r == rank). Collective: every rank constructs it with the same shape and dtype,
+    and every rank calls ``close()`` (peers unmap before owners free). The tensor must not be
+    used after ``close()``."""
+
+    def __init__(self, shape: tuple, dtype: torch.dtype, device: torch.device, group=None):
+        from . import _native
+        L = _native.lib()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.shape, self.dtype = tuple(shape), dtype
+        nbytes = torch.tensor([], dtype=dtype).element_size()
+        for d in self.shape:
+            nbytes *= d
+        with torch.cuda.device(device):
+            own = ctypes.c_void_p()
+            _native.check(L.g16_ipc_alloc(max(nbytes, 256), ctypes.byref(own)), "g16_ipc_alloc")
+            self._own = own.value
+            handle = ctypes.create_string_buffer(_native.IPC_HANDLE_BYTES)
+            _native.check(L.g16_ipc_get_handle(own, handle), "g16_ipc_get_handle")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            self.ptrs, self._opened = [], []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.ptrs.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                _native.check(L.g16_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(p)),
+                              "g16_ipc_open")
+                self.ptrs.append(p.value)
+                self._opened.append(p.value)
+            self.tensor = torch.as_tensor(_CudaArray(self._own, self.shape, dtype), device=device)
+
+    def close(self):
+        from . import _native
+        if self._own is None:
+            return
+        L = _native.lib()
+        torch.cuda.synchronize()
+        for p in self._opened:
+            _native.check(L.g16_ipc_close(ctypes.c_void_p(p)), "g16_ipc_close")
+        self._opened = []
+        dist.barrier(group=self.group)  # every peer has unmapped this rank's buffer
+        _native.check(L.g16_ipc_free(ctypes.c_void_p(self._own)), "g16_ipc_free")
+        self._own = None
+        self.tensor = None
+
+
 @dataclass
 class ShardedMatmul:
     """Column-sharded matmul with an all-gather of the output shards.
@@ -57,6 +124,8 @@ class ShardedMatmul:
     group: object = None
     out_dtype: torch.dtype = torch.float16
     local_mm: object = None
+    fused: bool | None = None  # None: the fused exchange whenever it applies (see the module doc)
+    _bufs: dict = field(default_factory=dict, repr=False)
 
     def __post_init__(self):
         self.world = dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -73,7 +142,52 @@ class ShardedMatmul:
     def local(self, a: torch.Tensor) -> torch.Tensor:
         return self.local_mm(a, self.w_shard)
 
+    def fused_applies(self, a: torch.Tensor) -> bool:
+        """The fused GEMM + exchange runs for fp16 CUDA activations with M > 8 over NCCL."""
+        if self.fused is False or self.world == 1 or not a.is_cuda:
+            return False
+        ok = (a.dtype == torch.float16 and a.dim() == 2 and a.shape[0] > 8 and self.w_shard.is_cuda
+              and self.w_shard.dtype == torch.float16 and self.out_dtype in (torch.float16, torch.float32)
+              and self.world <= 8 and dist.get_backend(self.group) == "nccl")
+        if self.fused and not ok:
+            raise ValueError("ShardedMatmul(fused=True) needs fp16 CUDA activations with M > 8 over NCCL "
+                             "(at most 8 ranks)")
+        return ok
+
+    def _fused_call(self, a: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+        from . import _native
+        a = a.contiguous()
+        M, K = a.shape
+        buf = self._bufs.get(M)
+        if buf is None:
+            buf = self._bufs[M] = PeerBuffer((M, self.n_total), self.out_dtype, a.device, self.group)
+            self._flag = torch.zeros(1, dtype=torch.int32, device=a.device)
+        # Peers are done with their outputs of the previous call before any tile lands there.
+        dist.all_reduce(self._flag, group=self.group)
+        ptrs = (ctypes.c_void_p * self.world)(*buf.ptrs)
+        st = _native.lib().g16_gemm_scatter(
+            a.data_ptr(), self.w_shard.data_ptr(), ptrs, self.world, _native.dtype_code(self.out_dtype), None,
+            None, M, K, self.n1 - self.n0, self.n_total, self.n0, _native.stream_handle(a.device.index or 0))
+        _native.check(st, "g16_gemm_scatter")
+        # Every peer's kernel (and so every tile it stored here) has completed.
+        dist.all_reduce(self._flag, group=self.group)
+        if out is not None:
+            out.copy_(buf.tensor)
+            return out
+        return buf.tensor
+
+    def close(self):
+        """Release the fused path's peer buffers (collective: every rank calls it)."""
+        for buf in self._bufs.values():
+            buf.close()
+        self._bufs.clear()
+
     def __call__(self, a: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The full [M, N] output on every rank. On the fused path the returned tensor is this
+        instance's output buffer for M rows: it stays valid until the next call with the same M
+        (or ``close()``); pass ``out`` to keep a copy."""
+        if self.fused_applies(a):
+            return self._fused_call(a, out)
         c_local = self.local(a).contiguous()
         M = a.shape[0]
         if self.world == 1:

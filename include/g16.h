@@ -122,6 +122,38 @@ int g16_gemm_static_scratch(const uint16_t* a16, const uint16_t* b16, void* out,
  * first cluster size tried, [6] at the chosen size. info must hold 7 ints. */
 int g16_skinny_plan(int M, int K, int N, int x_dtype, int* info);
 
+/*
+ * No counterpart in the reference (it has no multi-GPU path): the column-sharded GEMM with the
+ * output all-gather fused into the epilogue. This rank computes C = (a16[M,K] @ b16[K,N]) *
+ * rscale[row] + bias[col] for its N columns and stores every tile into each of the ndst buffers
+ * dst[d] (its own and its peers' full outputs, e.g. g16_ipc_open mappings over NVLink) at
+ * dst[d][row * ldc + col0 + col], with plain 16-byte stores of whole 128-byte row segments (no
+ * TMA, no multicast). No split-K. The caller orders the call against its peers: every rank must
+ * be done with its destination buffer before any peer's call starts, and a peer's stores are
+ * complete once that peer's kernel has completed (the grid ends with a system-scope fence).
+ * Requires 1 <= ndst <= G16_SCATTER_MAX_DST, K % 8 == 0, N % 8 == 0, col0 + N <= ldc, col0 and
+ * ldc multiples of 8, all pointers 16-byte aligned.
+ */
+#define G16_SCATTER_MAX_DST 8
+int g16_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
+                     const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
+                     void* stream);
+
+/*
+ * No counterpart in the reference: device buffers shared between the processes of one node with
+ * CUDA IPC, the destinations of g16_gemm_scatter. g16_ipc_alloc allocates `bytes` on the current
+ * device (cudaMalloc, so the buffer starts an allocation of its own and its handle maps it
+ * exactly); g16_ipc_get_handle writes its G16_IPC_HANDLE_BYTES-byte handle; another process opens
+ * it with g16_ipc_open (peer access enabled on first use) and releases it with g16_ipc_close
+ * before the owner calls g16_ipc_free.
+ */
+#define G16_IPC_HANDLE_BYTES 64
+int g16_ipc_alloc(size_t bytes, void** ptr);
+int g16_ipc_free(void* ptr);
+int g16_ipc_get_handle(void* ptr, void* handle);
+int g16_ipc_open(const void* handle, void** ptr);
+int g16_ipc_close(void* ptr);
+
 /* Device-side status word of the current device: G16_OK, or G16_ERR_TIMEOUT if a kernel's
  * bounded wait expired since the last clear. Synchronises `stream`. clear != 0 resets it. */
 int g16_device_status(int* status_out, int clear, void* stream);

@@ -1,7 +1,11 @@
-"""Column-sharded matmul across 2 GPUs over NCCL (skipped with fewer than 2 GPUs). The gathered
-output equals, bit for bit, the single-GPU results of the same column shards (same kernel, same
-shape, same K order); against the unsharded product it agrees within the GEMM tolerance (a shard
-can get a different automatic K split than the full matrix)."""
+"""Column-sharded matmul across 2 GPUs (skipped with fewer than 2 GPUs).
+
+Fused path (fp16 activations, M > 8, NCCL): every rank's GEMM epilogue stores its output tiles into
+both ranks' full output buffers (CUDA IPC over NVLink). The result equals, bit for bit, the same
+column shards computed on one GPU with g16_gemm and ksplit = 1 (same kernel, same K order), and the
+fp64 product within the GEMM tolerance; two calls in a row check the ordering of buffer reuse.
+Gather path (fused=False): mm_t per shard and one NCCL all-gather; equals the single-GPU shards.
+"""
 import os
 import socket
 
@@ -17,6 +21,18 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _shard_gemm_ksplit1(a, w_shard, out_dtype):
+    from gtx16_fp16 import _native
+    L = _native.lib()
+    M, K = a.shape
+    n = w_shard.shape[1]
+    out = torch.empty(M, n, dtype=out_dtype, device=a.device)
+    st = L.g16_gemm(a.data_ptr(), w_shard.data_ptr(), out.data_ptr(), _native.dtype_code(out_dtype), None, None,
+                    M, K, n, 1, None, 0, _native.stream_handle(a.device.index or 0))
+    _native.check(st, "g16_gemm")
+    return out
+
+
 def _worker(rank, world, port, ret):
     import datetime
 
@@ -29,23 +45,39 @@ def _worker(rank, world, port, ret):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
+    results = {}
     try:
+        for M, K, N, out_dtype in ((1024, 2048, 4096, torch.float16), (1000, 1024, 4104, torch.float32)):
+            gen = torch.Generator(device="cuda").manual_seed(M + N)
+            w = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
+            n0, n1 = shard_bounds(N, world, rank)
+            fused = ShardedMatmul(w[:, n0:n1].contiguous(), N, out_dtype=out_dtype)
+            for call in range(2):
+                a = torch.randn(M, K, device="cuda", generator=gen).half()
+                assert fused.fused_applies(a)
+                y = fused(a).clone()
+                shards = [_shard_gemm_ksplit1(a, w[:, b0:b1].contiguous(), out_dtype)
+                          for b0, b1 in (shard_bounds(N, world, r) for r in range(world))]
+                ref = a.double() @ w.double()
+                results[f"fused {M}x{K}x{N} {out_dtype} call {call} bitwise"] = torch.equal(y, torch.cat(shards, dim=1))
+                results[f"fused {M}x{K}x{N} {out_dtype} call {call} fp64"] = \
+                    ((y.double() - ref).norm() / ref.norm()).item() < 1e-3
+            fused.close()
+        # gather path (mm_t per shard + NCCL all-gather)
         gen = torch.Generator(device="cuda").manual_seed(0)
         M, K, N = 1024, 2048, 4096
         a = torch.randn(M, K, device="cuda", generator=gen).half()
         w = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
         n0, n1 = shard_bounds(N, world, rank)
-        y = ShardedMatmul(w[:, n0:n1].contiguous(), N)(a)
+        y = ShardedMatmul(w[:, n0:n1].contiguous(), N, fused=False)(a)
         shards = [g.mm_t(a, w[:, b0:b1].contiguous(), None, torch.float16)
                   for b0, b1 in (shard_bounds(N, world, r) for r in range(world))]
-        ok = torch.equal(y, torch.cat(shards, dim=1))
-        ref = a.double() @ w.double()
-        ok = ok and ((y.double() - ref).norm() / ref.norm()).item() < 1e-3
+        results["gather bitwise"] = torch.equal(y, torch.cat(shards, dim=1))
         full = g.mm_t(a, w, None, torch.float16)
         rows = gather_rows(full[batch_slice(M, world, rank)], M)
-        ok = ok and torch.equal(rows, full)
+        results["gather_rows"] = torch.equal(rows, full)
         torch.cuda.synchronize()
-        ret[rank] = bool(ok)
+        ret[rank] = results
     finally:
         dist.destroy_process_group()
 
@@ -56,4 +88,8 @@ def test_sharded_matmul_two_gpus():
     import torch.multiprocessing as mp
     ret = mp.Manager().dict()
     mp.spawn(_worker, args=(2, _free_port(), ret), nprocs=2, join=True)
-    assert dict(ret) == {0: True, 1: True}
+    got = dict(ret)
+    assert sorted(got) == [0, 1]
+    for rank, res in got.items():
+        bad = [k for k, v in res.items() if not v]
+        assert not bad, f"rank {rank}: {bad}"
