@@ -721,6 +721,9 @@ def main():
         return  # the reference arm is the host CPU path: rank 0 alone runs and prints it
     if world > 1 and args.impl == "ours":
         import torch.distributed as dist
+        # The only collectives are small (barrier all-reduces, result gathers): no NVLink multicast
+        # objects are needed, and none stay bound to a rank's memory.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local if world > 1 else 0)

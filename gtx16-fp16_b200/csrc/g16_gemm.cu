@@ -65,6 +65,17 @@ struct GemmArgs {
   int ksplit, kblocks, kb_per_split, units;
 };
 
+// Scatter epilogue modes.
+constexpr int kScatterNone = 0;
+constexpr int kScatterStores = 1;  // 16-byte stores by the epilogue warps
+constexpr int kScatterTma = 2;     // TMA tile stores of the staged rows, one per destination
+
+// Destination tensor maps of the TMA scatter epilogue: [M rows, col0 + N columns] of dst[d] with
+// row stride ldc, [32 x 128-byte] boxes, 128-byte swizzle (the staging layout).
+struct DstMaps {
+  CUtensorMap m[kMaxDst];
+};
+
 struct Unit {
   int tile, mt, nt, split, kb0, kb1;
 };
@@ -147,18 +158,18 @@ __device__ __forceinline__ void scatter_rows(const GemmArgs& a, const uint8_t* s
   }
 }
 
-template <bool OUT_F16, bool SCATTER>
+template <bool OUT_F16, int SCATTER>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-            const GemmArgs args) {
+            const GemmArgs args, const __grid_constant__ DstMaps dmaps) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
   // Align by pointer arithmetic on the __shared__ array (an integer round trip would turn
   // every access into a generic-address load).
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* stage_base = smem;
-  uint8_t* epi_stage = smem + kStages * kStageBytes;  // scatter only: kEpiStageBytes
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_stage + (SCATTER ? kEpiStageBytes : 0));
+  uint8_t* epi_stage = smem + kStages * kStageBytes;  // scatter only: kEpiStageBytes, 1 KiB aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_stage + (SCATTER != kScatterNone ? kEpiStageBytes : 0));
   uint64_t* empty_bar = full_bar + kStages;
   uint64_t* tfull_bar = empty_bar + kStages;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -291,7 +302,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       if (!got && lane == 0) report_timeout(args.status, abort_flag);
       const int row = w.mt * kBM + r_local;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
-      if constexpr (SCATTER) {
+      if constexpr (SCATTER != kScatterNone) {
         // ksplit == 1 (enforced by the launcher). 128 bytes per row per pass: 64 fp16 or 32 fp32
         // columns; every destination gets each row segment once.
         if (!got) break;
@@ -336,13 +347,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
               }
             }
           }
-          // this lane's row: 8 chunks of 16 bytes, swizzled by row
+          // this lane's row: 8 chunks of 16 bytes, swizzled by row (the 128-byte TMA swizzle)
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             *reinterpret_cast<uint4*>(my_stage + lane * 128 + ((j ^ (lane & 7)) << 4)) = packed[j];
-          __syncwarp();
-          scatter_rows<OUT_F16>(args, my_stage, w.mt * kBM + quarter * 32, gcol, lane);
-          __syncwarp();  // the stage is rewritten by the next pass
+          if constexpr (SCATTER == kScatterTma) {
+            fence_proxy_async_smem();  // staged rows -> visible to the TMA engine
+            __syncwarp();
+            const int y = w.mt * kBM + quarter * 32;
+            if (lane == 0 && y < args.M && gcol < args.N) {
+              for (int d = 0; d < args.ndst; ++d) tma_store_2d(&dmaps.m[d], my_stage, args.col0 + gcol, y);
+              bulk_commit_group();
+              bulk_wait_group_read0();  // the engine has read the stage: it may be rewritten
+            }
+            __syncwarp();
+          } else {
+            __syncwarp();
+            scatter_rows<OUT_F16>(args, my_stage, w.mt * kBM + quarter * 32, gcol, lane);
+            __syncwarp();  // the stage is rewritten by the next pass
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -391,8 +414,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     }
   }
 
-  // Scatter: stores into peer memory (NVLink) are made visible system-wide before the grid ends.
-  if constexpr (SCATTER) __threadfence_system();
+  // Scatter: stores into peer memory (NVLink) are complete and visible system-wide before the grid
+  // ends.
+  if constexpr (SCATTER == kScatterTma) {
+    if (warp >= 2 && lane == 0) bulk_wait_group0();
+  }
+  if constexpr (SCATTER != kScatterNone) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -495,7 +522,7 @@ cudaError_t ensure_smem_attr(F* kern, std::atomic<uint64_t>& done, int bytes) {
   return e;
 }
 
-std::atomic<uint64_t> g_attr_f16{0}, g_attr_f32{0}, g_attr_sc16{0}, g_attr_sc32{0};
+std::atomic<uint64_t> g_attr_f16{0}, g_attr_f32{0}, g_attr_sc16{0}, g_attr_sc32{0}, g_attr_tm16{0}, g_attr_tm32{0};
 
 template <bool OUT_F16>
 cudaError_t launch_reduce(const GemmArgs& args, cudaStream_t s, const DeviceInfo& dev) {
@@ -560,14 +587,15 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
 
   const int grid = args.units < dev.sm_count ? args.units : dev.sm_count;
   cudaError_t e;
+  static const DstMaps kNoMaps{};
   if (out_dtype == G16_F16) {
-    e = ensure_smem_attr(gemm_kernel<true, false>, g_attr_f16, static_cast<int>(kSmemBytes));
+    e = ensure_smem_attr(gemm_kernel<true, kScatterNone>, g_attr_f16, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return cuda_fail(e);
-    gemm_kernel<true, false><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
+    gemm_kernel<true, kScatterNone><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args, kNoMaps);
   } else {
-    e = ensure_smem_attr(gemm_kernel<false, false>, g_attr_f32, static_cast<int>(kSmemBytes));
+    e = ensure_smem_attr(gemm_kernel<false, kScatterNone>, g_attr_f32, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return cuda_fail(e);
-    gemm_kernel<false, false><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args);
+    gemm_kernel<false, kScatterNone><<<grid, kThreads, kSmemBytes, s>>>(ta, tb, args, kNoMaps);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
@@ -582,7 +610,7 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
 
 int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
                         const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
-                        cudaStream_t s, const DeviceInfo& dev) {
+                        int flags, cudaStream_t s, const DeviceInfo& dev) {
   if (ndst < 1 || ndst > kMaxDst) return G16_ERR_ARG;
   if (M <= 0 || N <= 0) return G16_OK;
   GemmArgs args{};
@@ -615,16 +643,42 @@ int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* d
   st = make_tmap_2d(&tb, b16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                     kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
+  const bool tma = flags == G16_SCATTER_TMA;
+  DstMaps maps{};
+  if (tma) {
+    // [M, col0 + N] of each destination: columns past this rank's shard are outside the map, so a
+    // partial last box cannot spill into a neighbour's columns.
+    for (int d = 0; d < ndst; ++d) {
+      st = make_tmap_2d_strided(&maps.m[d], dst[d],
+                                out_dtype == G16_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                out_dtype == G16_F16 ? 2 : 4, static_cast<uint64_t>(M),
+                                static_cast<uint64_t>(col0) + static_cast<uint64_t>(N), static_cast<uint64_t>(ldc), 32,
+                                out_dtype == G16_F16 ? 64 : 32, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (st != G16_OK) return st;
+    }
+  }
   const int grid = args.units < dev.sm_count ? args.units : dev.sm_count;
   cudaError_t e;
   if (out_dtype == G16_F16) {
-    e = ensure_smem_attr(gemm_kernel<true, true>, g_attr_sc16, static_cast<int>(kSmemBytesScatter));
-    if (e != cudaSuccess) return cuda_fail(e);
-    gemm_kernel<true, true><<<grid, kThreads, kSmemBytesScatter, s>>>(ta, tb, args);
+    if (tma) {
+      e = ensure_smem_attr(gemm_kernel<true, kScatterTma>, g_attr_tm16, static_cast<int>(kSmemBytesScatter));
+      if (e != cudaSuccess) return cuda_fail(e);
+      gemm_kernel<true, kScatterTma><<<grid, kThreads, kSmemBytesScatter, s>>>(ta, tb, args, maps);
+    } else {
+      e = ensure_smem_attr(gemm_kernel<true, kScatterStores>, g_attr_sc16, static_cast<int>(kSmemBytesScatter));
+      if (e != cudaSuccess) return cuda_fail(e);
+      gemm_kernel<true, kScatterStores><<<grid, kThreads, kSmemBytesScatter, s>>>(ta, tb, args, maps);
+    }
   } else {
-    e = ensure_smem_attr(gemm_kernel<false, true>, g_attr_sc32, static_cast<int>(kSmemBytesScatter));
-    if (e != cudaSuccess) return cuda_fail(e);
-    gemm_kernel<false, true><<<grid, kThreads, kSmemBytesScatter, s>>>(ta, tb, args);
+    if (tma) {
+      e = ensure_smem_attr(gemm_kernel<false, kScatterTma>, g_attr_tm32, static_cast<int>(kSmemBytesScatter));
+      if (e != cudaSuccess) return cuda_fail(e);
+      gemm_kernel<false, kScatterTma><<<grid, kThreads, kSmemBytesScatter, s>>>(ta, tb, args, maps);
+    } else {
+      e = ensure_smem_attr(gemm_kernel<false, kScatterStores>, g_attr_sc32, static_cast<int>(kSmemBytesScatter));
+      if (e != cudaSuccess) return cuda_fail(e);
+      gemm_kernel<false, kScatterStores><<<grid, kThreads, kSmemBytesScatter, s>>>(ta, tb, args, maps);
+    }
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);

@@ -48,10 +48,13 @@ size_t gemm_workspace_bytes(int M, int K, int N, int ksplit);
 // Sharded GEMM whose fp16/fp32 output tiles go to ndst buffers [M, ldc] at column col0 (no split-K).
 int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
                         const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
-                        cudaStream_t s, const DeviceInfo& dev);
+                        int flags, cudaStream_t s, const DeviceInfo& dev);
 int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
 
 // 2-D TMA tensor map over a row-major [rows, cols] matrix with a [box_rows, box_cols] box (g16_tmap.cu).
+int make_tmap_2d_strided(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes,
+                         uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_rows, uint32_t box_cols,
+                         CUtensorMapSwizzle swz);
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes, uint64_t rows,
                  uint64_t cols, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swz);
 

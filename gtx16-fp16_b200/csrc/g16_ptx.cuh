@@ -154,6 +154,20 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const void* des
       : "memory");
 }
 
+// Tile store shared -> global through a tensor map, tracked by bulk async-groups (no multicast).
+// Out-of-range parts of the box are not written. x = innermost (column) coordinate.
+__device__ __forceinline__ void tma_store_2d(const void* desc, const void* smem_src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The shared-memory sources of this thread's committed groups have been read (may be rewritten).
+__device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's committed groups have completed (their writes are performed).
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // L2 eviction-priority policies for the cache_hint operand (createpolicy.fractional).
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;

@@ -27,6 +27,7 @@ _lock = threading.Lock()
 _P, _I, _F, _Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
 IPC_HANDLE_BYTES = 64       # G16_IPC_HANDLE_BYTES
 SCATTER_MAX_DST = 8         # G16_SCATTER_MAX_DST
+SCATTER_DEFAULT, SCATTER_STORES, SCATTER_TMA = 0, 1, 2  # G16_SCATTER_* store methods
 SIGNATURES = {
     "g16_mm_t": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "g16_mm_t_workspace_bytes": (_Z, [_I, _I, _I, _I]),
@@ -36,7 +37,8 @@ SIGNATURES = {
     "g16_gemm_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g16_gemm_auto_ksplit": (_I, [_I, _I, _I]),
     "g16_gemm_static_scratch": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P]),
-    "g16_gemm_scatter": (_I, [_P, _P, ctypes.POINTER(_P), _I, _I, _P, _P, _I, _I, _I, ctypes.c_longlong, _I, _P]),
+    "g16_gemm_scatter": (_I, [_P, _P, ctypes.POINTER(_P), _I, _I, _P, _P, _I, _I, _I, ctypes.c_longlong, _I, _I,
+                              _P]),
     "g16_ipc_alloc": (_I, [_Z, ctypes.POINTER(_P)]),
     "g16_ipc_free": (_I, [_P]),
     "g16_ipc_get_handle": (_I, [_P, _P]),

@@ -125,6 +125,7 @@ class ShardedMatmul:
     out_dtype: torch.dtype = torch.float16
     local_mm: object = None
     fused: bool | None = None  # None: the fused exchange whenever it applies (see the module doc)
+    scatter_flags: int = 0     # G16_SCATTER_* store method of the fused path (0: the library's default)
     _bufs: dict = field(default_factory=dict, repr=False)
 
     def __post_init__(self):
@@ -167,7 +168,8 @@ class ShardedMatmul:
         ptrs = (ctypes.c_void_p * self.world)(*buf.ptrs)
         st = _native.lib().g16_gemm_scatter(
             a.data_ptr(), self.w_shard.data_ptr(), ptrs, self.world, _native.dtype_code(self.out_dtype), None,
-            None, M, K, self.n1 - self.n0, self.n_total, self.n0, _native.stream_handle(a.device.index or 0))
+            None, M, K, self.n1 - self.n0, self.n_total, self.n0, self.scatter_flags,
+            _native.stream_handle(a.device.index or 0))
         _native.check(st, "g16_gemm_scatter")
         # Every peer's kernel (and so every tile it stored here) has completed.
         dist.all_reduce(self._flag, group=self.group)

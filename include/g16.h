@@ -127,17 +127,22 @@ int g16_skinny_plan(int M, int K, int N, int x_dtype, int* info);
  * output all-gather fused into the epilogue. This rank computes C = (a16[M,K] @ b16[K,N]) *
  * rscale[row] + bias[col] for its N columns and stores every tile into each of the ndst buffers
  * dst[d] (its own and its peers' full outputs, e.g. g16_ipc_open mappings over NVLink) at
- * dst[d][row * ldc + col0 + col], with plain 16-byte stores of whole 128-byte row segments (no
- * TMA, no multicast). No split-K. The caller orders the call against its peers: every rank must
+ * dst[d][row * ldc + col0 + col], in whole 128-byte row segments (no multicast). No split-K. The caller orders the call against its peers: every rank must
  * be done with its destination buffer before any peer's call starts, and a peer's stores are
  * complete once that peer's kernel has completed (the grid ends with a system-scope fence).
  * Requires 1 <= ndst <= G16_SCATTER_MAX_DST, K % 8 == 0, N % 8 == 0, col0 + N <= ldc, col0 and
  * ldc multiples of 8, all pointers 16-byte aligned.
  */
 #define G16_SCATTER_MAX_DST 8
+/* flags: how the tiles reach the destinations. G16_SCATTER_DEFAULT picks the measured best;
+ * G16_SCATTER_STORES: 16-byte stores by the epilogue warps; G16_SCATTER_TMA: one TMA tile store
+ * (cp.async.bulk.tensor, shared -> global) per destination from the staged rows. */
+#define G16_SCATTER_DEFAULT 0
+#define G16_SCATTER_STORES 1
+#define G16_SCATTER_TMA 2
 int g16_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
                      const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
-                     void* stream);
+                     int flags, void* stream);
 
 /*
  * No counterpart in the reference: device buffers shared between the processes of one node with

@@ -29,7 +29,8 @@ def _gemm_ksplit1(a, b, bias, out_dtype):
                                              (129, 520, 264, 1024, 528), (4096, 4096, 512, 4096, 3584)])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 @pytest.mark.parametrize("with_bias", [False, True])
-def test_scatter_matches_gemm(cuda_ok, M, K, N, ldc, col0, out_dtype, with_bias):
+@pytest.mark.parametrize("flags", [0, 1, 2])
+def test_scatter_matches_gemm(cuda_ok, M, K, N, ldc, col0, out_dtype, with_bias, flags):
     gen = torch.Generator(device="cuda").manual_seed(M + N + col0)
     a = torch.randn(M, K, device="cuda", generator=gen).half()
     b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
@@ -39,7 +40,7 @@ def test_scatter_matches_gemm(cuda_ok, M, K, N, ldc, col0, out_dtype, with_bias)
     ptrs = (ctypes.c_void_p * 2)(*[d.data_ptr() for d in dsts])
     st = _native.lib().g16_gemm_scatter(a.data_ptr(), b.data_ptr(), ptrs, 2, _native.dtype_code(out_dtype),
                                         None if bias is None else bias.data_ptr(), None, M, K, N, ldc, col0,
-                                        _native.stream_handle(0))
+                                        flags, _native.stream_handle(0))
     _native.check(st, "g16_gemm_scatter")
     ref = _gemm_ksplit1(a, b, bias, out_dtype)
     torch.cuda.synchronize()
@@ -57,10 +58,11 @@ def test_scatter_rejects_bad_arguments(cuda_ok):
     one = (ctypes.c_void_p * 1)(d.data_ptr())
     s = _native.stream_handle(0)
     f16 = _native.G16_F16
-    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 0, f16, None, None, 256, 64, 64, 128, 0, s) == _native.ERR_ARG
-    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 9, f16, None, None, 256, 64, 64, 128, 0, s) == _native.ERR_ARG
-    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 68, s) == _native.ERR_ARG
-    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 4, s) == \
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 0, f16, None, None, 256, 64, 64, 128, 0, 0, s) == _native.ERR_ARG
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 9, f16, None, None, 256, 64, 64, 128, 0, 0, s) == _native.ERR_ARG
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 68, 0, s) == _native.ERR_ARG
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 4, 0, s) == \
         _native.ERR_UNSUPPORTED
     mis = (ctypes.c_void_p * 1)(d.data_ptr() + 8)
-    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), mis, 1, f16, None, None, 256, 64, 64, 128, 0, s) == _native.ERR_ALIGN
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), mis, 1, f16, None, None, 256, 64, 64, 128, 0, 0, s) == _native.ERR_ALIGN
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 0, 3, s) == _native.ERR_ARG

@@ -73,9 +73,10 @@ def test_argument_checks_return_codes_without_launching():
     assert L.g16_skinny(p16, 0, p16, None, p16, 0, 9, 8, 8, None) == _native.ERR_ARG
     assert L.g16_rowscale(p16, 0, p16, p16, 2, 12, 1024.0, None) == _native.ERR_UNSUPPORTED
     dsts = (ctypes.c_void_p * 1)(p16)
-    assert L.g16_gemm_scatter(p16, p16, dsts, 0, 1, None, None, 16, 8, 8, 8, 0, None) == _native.ERR_ARG
-    assert L.g16_gemm_scatter(p16, p16, dsts, 1, 1, None, None, 16, 12, 8, 8, 0, None) == _native.ERR_UNSUPPORTED
-    assert L.g16_gemm_scatter(p16, p16, dsts, 1, 1, None, None, 16, 8, 8, 8, 8, None) == _native.ERR_ARG
+    assert L.g16_gemm_scatter(p16, p16, dsts, 0, 1, None, None, 16, 8, 8, 8, 0, 0, None) == _native.ERR_ARG
+    assert L.g16_gemm_scatter(p16, p16, dsts, 1, 1, None, None, 16, 12, 8, 8, 0, 0, None) == _native.ERR_UNSUPPORTED
+    assert L.g16_gemm_scatter(p16, p16, dsts, 1, 1, None, None, 16, 8, 8, 8, 8, 0, None) == _native.ERR_ARG
+    assert L.g16_gemm_scatter(p16, p16, dsts, 1, 1, None, None, 16, 8, 8, 8, 0, 5, None) == _native.ERR_ARG
     assert L.g16_ipc_alloc(0, None) == _native.ERR_ARG
     assert L.g16_ipc_open(None, None) == _native.ERR_ARG
     assert L.g16_launch_count() == 0
