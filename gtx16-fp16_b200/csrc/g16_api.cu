@@ -222,7 +222,8 @@ int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, voi
   }
   // fp16 activations need no rescale here: products accumulate in fp32 TMEM and cannot overflow
   // the way the reference's fp16 partial sums could.
-  return launch_gemm(a16, static_cast<const uint16_t*>(w_t), out, out_dtype, bias, rscale, M, K, N, L.ksplit,
+  // ksplit 0: the automatic plan (L.ksplit sized the workspace for its fallback).
+  return launch_gemm(a16, static_cast<const uint16_t*>(w_t), out, out_dtype, bias, rscale, M, K, N, 0,
                      L.ksplit > 1 ? ws : nullptr, L.partials_bytes, s, *dev);
 }
 
@@ -259,7 +260,6 @@ int g16_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype,
   if (bias != nullptr && !aligned16(bias)) return G16_ERR_ALIGN;
   const DeviceInfo* dev = device_info(&st);
   if (dev == nullptr) return st;
-  if (ksplit == 0) ksplit = gemm_auto_ksplit(M, K, N, *dev);
   return launch_gemm(a16, b16, out, out_dtype, bias, rscale, M, K, N, ksplit, workspace, workspace_bytes,
                      static_cast<cudaStream_t>(stream), *dev);
 }
@@ -324,6 +324,18 @@ int g16_ipc_close(void* ptr) {
   if (ptr == nullptr) return G16_ERR_ARG;
   cudaError_t e = cudaIpcCloseMemHandle(ptr);
   return e == cudaSuccess ? G16_OK : cuda_fail(e);
+}
+
+int g16_gemm_plan(int M, int K, int N, int* info) {
+  if (info == nullptr || M <= 0 || K <= 0 || N <= 0) return G16_ERR_ARG;
+  int st = G16_OK;
+  const DeviceInfo* dev = device_info(&st);
+  if (dev == nullptr) return st;
+  const SmallPlan p = plan_gemm_small(M, K, N, *dev);
+  info[0] = p.bn != 0 ? 1 : 0;
+  info[1] = p.bn != 0 ? p.bn : kBN;
+  info[2] = p.bn != 0 ? p.csize : gemm_auto_ksplit(M, K, N, *dev);
+  return G16_OK;
 }
 
 int g16_skinny_plan(int M, int K, int N, int x_dtype, int* info) {

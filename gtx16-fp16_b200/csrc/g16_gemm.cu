@@ -550,8 +550,20 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
                 const DeviceInfo& dev) {
   if (M <= 0 || N <= 0) return G16_OK;
   const int kblocks = (K + kBK - 1) / kBK;
-  if (ksplit < 1) ksplit = 1;
+  if (ksplit == 0) {
+    const SmallPlan p = plan_gemm_small(M, K, N, dev);
+    if (p.bn != 0) {
+      const int st = launch_gemm_small(a16, b16, out, out_dtype, bias, rscale, M, K, N, p.bn, p.csize, false, s);
+      if (st != G16_ERR_UNSUPPORTED) return st;
+    }
+    ksplit = gemm_auto_ksplit(M, K, N, dev);
+  }
   if (ksplit > kblocks) ksplit = kblocks;
+  if (ksplit > 1 && ksplit <= 16) {
+    const int st = launch_gemm_small(a16, b16, out, out_dtype, bias, rscale, M, K, N, 256, ksplit, true, s);
+    if (st != G16_ERR_UNSUPPORTED) return st;
+  }
+  if (ksplit < 1) ksplit = 1;
   GemmArgs args{};
   args.out = out;
   args.bias = bias;

@@ -40,7 +40,11 @@ int skinny_plan_info(int M, int K, int N, int x_dtype, int* info, const DeviceIn
 int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M, int K, float thresh,
                     cudaStream_t s);
 
-// Tensor-core GEMM. ws must hold gemm_workspace_bytes(M, K, N, ksplit) when ksplit > 1.
+// Tensor-core GEMM. ksplit = 0: automatic plan (the small-problem kernel when the output has too
+// few tiles for the persistent one; ws must still hold gemm_workspace_bytes(M, K, N,
+// gemm_auto_ksplit(...)) for the fallback). ksplit 2..16: that many K chunks reduced in a cluster
+// (same chunks and order as the workspace path, which runs when such a cluster cannot be resident
+// or ksplit > 16; ws must then hold gemm_workspace_bytes(M, K, N, ksplit)).
 int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                 const float* rscale, int M, int K, int N, int ksplit, void* ws, size_t ws_bytes, cudaStream_t s,
                 const DeviceInfo& dev);
@@ -50,6 +54,17 @@ int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* d
                         const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
                         int flags, cudaStream_t s, const DeviceInfo& dev);
 int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
+
+// Small-problem GEMM (g16_gemm_small.cu): one CTA per (tile, K chunk), K chunks of a tile reduced
+// inside a thread-block cluster. bn = 0: the problem has enough tiles for the persistent kernel.
+struct SmallPlan {
+  int bn = 0;     // 128 or 256 (N width of a tile)
+  int csize = 1;  // K chunks = cluster size
+};
+SmallPlan plan_gemm_small(int M, int K, int N, const DeviceInfo& dev);
+// exact: fail with G16_ERR_UNSUPPORTED rather than run fewer K chunks than csize.
+int launch_gemm_small(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                      const float* rscale, int M, int K, int N, int bn, int csize, bool exact, cudaStream_t s);
 
 // 2-D TMA tensor map over a row-major [rows, cols] matrix with a [box_rows, box_cols] box (g16_tmap.cu).
 int make_tmap_2d_strided(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes,

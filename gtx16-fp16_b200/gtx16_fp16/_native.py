@@ -44,6 +44,7 @@ SIGNATURES = {
     "g16_ipc_get_handle": (_I, [_P, _P]),
     "g16_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
     "g16_ipc_close": (_I, [_P]),
+    "g16_gemm_plan": (_I, [_I, _I, _I, ctypes.POINTER(_I)]),
     "g16_skinny_plan": (_I, [_I, _I, _I, _I, ctypes.POINTER(_I)]),
     "g16_device_status": (_I, [ctypes.POINTER(_I), _I, _P]),
     "g16_launch_count": (ctypes.c_uint64, []),

@@ -182,9 +182,10 @@ def test_is_affected_reports_bool(cuda_ok):
 
 
 @pytest.mark.parametrize("M,K,N", [(64, 1024, 1024), (128, 16384, 1024), (300, 4096, 256), (129, 2048, 8)])
-@pytest.mark.parametrize("ksplit", [1, 2, 3, 7, 16])
+@pytest.mark.parametrize("ksplit", [1, 2, 3, 5, 7, 13, 16, 20])
 def test_forced_split_k_through_c_abi(cuda_ok, M, K, N, ksplit):
-    """g16_gemm with a forced K split: deterministic last-arriver reduction matches fp64."""
+    """g16_gemm with a forced K split (2..16: chunks reduced inside a thread-block cluster; 20: through
+    the workspace): deterministic, matches fp64."""
     torch.manual_seed(ksplit)
     a = torch.randn(M, K, device="cuda").half()
     b = (torch.randn(K, N, device="cuda") * K ** -0.5).half()
@@ -202,6 +203,42 @@ def test_forced_split_k_through_c_abi(cuda_ok, M, K, N, ksplit):
         outs.append(out)
     assert torch.equal(outs[0], outs[1])
     assert_close_fp64(outs[0], a, b, bias, torch.float32, f"split {ksplit}")
+
+
+def _gemm_c(a, b, bias, rscale, out_dtype, ksplit):
+    L = _native.lib()
+    M, K = a.shape
+    N = b.shape[1]
+    nws = int(L.g16_gemm_workspace_bytes(M, K, N, ksplit))
+    ws = torch.empty(max(nws, 256), dtype=torch.uint8, device="cuda")
+    out = torch.empty(M, N, device="cuda", dtype=out_dtype)
+    st = L.g16_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), _native.dtype_code(out_dtype),
+                    None if bias is None else bias.data_ptr(), None if rscale is None else rscale.data_ptr(),
+                    M, K, N, ksplit, ws.data_ptr(), ws.numel(), _native.stream_handle(0))
+    assert st == 0, _native.strerror(st)
+    return out
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 16384, 1024), (2048, 3072, 1024), (1000, 4096, 392), (250, 8192, 2000),
+                                   (64, 1024, 1024), (384, 512, 136)])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_automatic_small_problem_plan(cuda_ok, M, K, N, out_dtype):
+    """ksplit = 0 on outputs with few tiles: one CTA per (tile, K chunk), chunks reduced in a cluster.
+    Deterministic, and within the GEMM tolerance of fp64 (with bias and per-row unscale), as is the
+    forced single pass on the same inputs."""
+    gen = torch.Generator(device="cuda").manual_seed(M + N)
+    a = torch.randn(M, K, device="cuda", generator=gen).half()
+    b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
+    bias = torch.randn(N, device="cuda", generator=gen)
+    rscale = torch.where(torch.rand(M, device="cuda", generator=gen) < 0.1, 4.0, 1.0)
+    y0 = _gemm_c(a, b, bias, rscale, out_dtype, 0)
+    y1 = _gemm_c(a, b, bias, rscale, out_dtype, 0)
+    assert torch.equal(y0, y1)
+    single = _gemm_c(a, b, bias, rscale, out_dtype, 1)
+    ref = (a.double() @ b.double()) * rscale.double()[:, None] + bias.double()
+    for y, what in ((y0, "automatic"), (single, "single pass")):
+        assert torch.isfinite(y).all()
+        assert ((y.double() - ref).norm() / ref.norm()).item() < GEMM_NORM, what
 
 
 def test_rowscale_through_c_abi(cuda_ok):
