@@ -63,6 +63,9 @@ struct GemmArgs {
   int M, N, K;
   int m_tiles, n_tiles, tiles;
   int ksplit, kblocks, kb_per_split, units;
+  // Tail split (ksplit == 1): units >= full_units are 128-column halves of the last tiles, so a
+  // last partial wave of T tiles runs as 2T half-tiles on the idle SMs (full K, no reduction).
+  int full_units, split_tail;
 };
 
 // Scatter epilogue modes.
@@ -78,12 +81,21 @@ struct DstMaps {
 
 struct Unit {
   int tile, mt, nt, split, kb0, kb1;
+  int col0, ncols;  // first output column and width of the unit (kBN, or 128 for a tail half)
 };
 
 __device__ __forceinline__ Unit unit_coords(const GemmArgs& a, int u) {
   Unit r;
-  r.tile = u / a.ksplit;
-  r.split = u - r.tile * a.ksplit;
+  int half = -1;
+  if (a.split_tail && u >= a.full_units) {
+    const int h = u - a.full_units;
+    r.tile = a.full_units + (h >> 1);
+    r.split = 0;
+    half = h & 1;
+  } else {
+    r.tile = u / a.ksplit;
+    r.split = u - r.tile * a.ksplit;
+  }
   // Grouped rasterisation: walk kGroupM tile-rows together so B column panels stay in L2.
   const int per_group = kGroupM * a.n_tiles;
   const int g = r.tile / per_group;
@@ -94,6 +106,8 @@ __device__ __forceinline__ Unit unit_coords(const GemmArgs& a, int u) {
   r.nt = in_g / gsize;
   r.kb0 = r.split * a.kb_per_split;
   r.kb1 = min(a.kblocks, r.kb0 + a.kb_per_split);
+  r.col0 = r.nt * kBN + (half > 0 ? kBN / 2 : 0);
+  r.ncols = half >= 0 ? kBN / 2 : kBN;
   return r;
 }
 
@@ -230,13 +244,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           }
           uint8_t* sa = stage_base + stage * kStageBytes;
           uint8_t* sb = sa + kABytes;
-          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+          const int nbox = w.ncols / 64;
+          mbar_arrive_expect_tx(&full_bar[stage], kABytes + nbox * kBBoxBytes);
           armed[stage] = true;
           armed_phase[stage] = phase;
           tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * kBK, w.mt * kBM);
-#pragma unroll
-          for (int j = 0; j < kBN / 64; ++j)
-            tma_load_2d(sb + j * kBBoxBytes, &tmap_b, &full_bar[stage], w.nt * kBN + 64 * j, kb * kBK);
+          for (int j = 0; j < nbox; ++j)
+            tma_load_2d(sb + j * kBBoxBytes, &tmap_b, &full_bar[stage], w.col0 + 64 * j, kb * kBK);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
       }
@@ -250,7 +264,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN, /*b_mn_major=*/true);
+      constexpr uint32_t idesc_full = idesc_f16_f32(kBM, kBN, /*b_mn_major=*/true);
+      constexpr uint32_t idesc_half = idesc_f16_f32(kBM, kBN / 2, /*b_mn_major=*/true);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -261,6 +276,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        const uint32_t idesc = w.ncols == kBN ? idesc_full : idesc_half;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
@@ -311,8 +327,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         constexpr int kCols = OUT_F16 ? 64 : 32;
         uint8_t* my_stage = epi_stage + quarter * (32 * 128);
 #pragma unroll 1
-        for (int c0 = 0; c0 < kBN; c0 += kCols) {
-          const int gcol = w.nt * kBN + c0;  // local column of the pass
+        for (int c0 = 0; c0 < w.ncols; c0 += kCols) {
+          const int gcol = w.col0 + c0;  // local column of the pass
           uint4 packed[8];
 #pragma unroll
           for (int h = 0; h < kCols / 32; ++h) {
@@ -375,7 +391,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         tc_fence_after();
         const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = 0; c < w.ncols / 32; ++c) {
           uint32_t r[32];
           __syncwarp();
           tmem_ld_32x32b_x32(t_row + c * 32, r);
@@ -383,7 +399,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          store_row32<OUT_F16>(args, row, w.nt * kBN + c * 32, rs, v);
+          store_row32<OUT_F16>(args, row, w.col0 + c * 32, rs, v);
         }
         tc_fence_before();
         __syncwarp();
@@ -522,6 +538,18 @@ cudaError_t ensure_smem_attr(F* kern, std::atomic<uint64_t>& done, int bytes) {
   return e;
 }
 
+// A last partial wave of at most half the SMs runs as 128-column halves (see GemmArgs).
+void set_tail_split(GemmArgs& a, const DeviceInfo& dev) {
+  a.full_units = a.units;
+  a.split_tail = 0;
+  if (a.ksplit != 1 || a.tiles <= dev.sm_count) return;
+  const int tail = a.tiles % dev.sm_count;
+  if (tail == 0 || 2 * tail > dev.sm_count) return;
+  a.split_tail = 1;
+  a.full_units = a.tiles - tail;
+  a.units = a.full_units + 2 * tail;
+}
+
 std::atomic<uint64_t> g_attr_f16{0}, g_attr_f32{0}, g_attr_sc16{0}, g_attr_sc32{0}, g_attr_tm16{0}, g_attr_tm32{0};
 
 template <bool OUT_F16>
@@ -581,6 +609,7 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
   ksplit = (kblocks + args.kb_per_split - 1) / args.kb_per_split;  // no empty splits
   args.ksplit = ksplit;
   args.units = args.tiles * ksplit;
+  set_tail_split(args, dev);
   if (ksplit > 1) {
     const size_t need = partial_bytes(args.tiles, ksplit);
     if (ws == nullptr || ws_bytes < need) return G16_ERR_WORKSPACE;
@@ -647,6 +676,7 @@ int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* d
   args.kb_per_split = args.kblocks;
   args.ksplit = 1;
   args.units = args.tiles;
+  set_tail_split(args, dev);
 
   CUtensorMap ta, tb;
   int st = make_tmap_2d(&ta, a16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(M),

@@ -241,6 +241,22 @@ def test_automatic_small_problem_plan(cuda_ok, M, K, N, out_dtype):
         assert ((y.double() - ref).norm() / ref.norm()).item() < GEMM_NORM, what
 
 
+@pytest.mark.parametrize("M,K,N", [(4096, 1024, 4096), (2048, 512, 5120), (1000, 520, 5000)])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_persistent_gemm_split_tail(cuda_ok, M, K, N, out_dtype):
+    """Outputs whose last partial wave of 128 x 256 tiles fits in half the SMs: those tiles run as
+    128-column halves (512 tiles on 148 SMs: the last 68 as 136 halves). Deterministic, within the
+    GEMM tolerance, bias on every column including the ragged last tile."""
+    gen = torch.Generator(device="cuda").manual_seed(M + K + N)
+    a = torch.randn(M, K, device="cuda", generator=gen).half()
+    b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
+    bias = torch.randn(N, device="cuda", generator=gen)
+    y0 = _gemm_c(a, b, bias, None, out_dtype, 1)
+    y1 = _gemm_c(a, b, bias, None, out_dtype, 1)
+    assert torch.equal(y0, y1)
+    assert_close_fp64(y0, a, b, bias, out_dtype, "split tail")
+
+
 def test_rowscale_through_c_abi(cuda_ok):
     torch.manual_seed(5)
     M, K = 64, 1024

@@ -26,7 +26,8 @@ def _gemm_ksplit1(a, b, bias, out_dtype):
 
 
 @pytest.mark.parametrize("M,K,N,ldc,col0", [(1024, 2048, 2048, 4096, 2048), (1000, 1024, 2056, 4104, 0),
-                                             (129, 520, 264, 1024, 528), (4096, 4096, 512, 4096, 3584)])
+                                             (129, 520, 264, 1024, 528), (4096, 4096, 512, 4096, 3584),
+                                             (2048, 256, 5120, 6144, 1024)])  # last: split tail
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 @pytest.mark.parametrize("with_bias", [False, True])
 @pytest.mark.parametrize("flags", [0, 1, 2])
