@@ -1,0 +1,377 @@
+// Tensor-core GEMM on CTA pairs: out[M,N] = (A @ B) * rscale[row] + bias[col], A [M,K] fp16
+// K-major, B [K,N] fp16 N-major, fp32 accumulation in TMEM. Persistent, one cluster of 2 CTAs
+// (2 SMs) per 256 x 256 output tile:
+//   * each CTA of the pair loads its 128 rows of A and its 128-column half of B per 64-wide K step
+//     (32 KiB, against 48 KiB for a 128 x 256 tile on one SM: the operand bytes per FLOP drop by a
+//     third, and the single-SM kernel is close to the per-SM operand-load limit);
+//   * the leader CTA (rank 0 of the pair) issues tcgen05.mma.cta_group::2 (M = 256, N = 256,
+//     K = 16), which reads A and B from both CTAs' shared memory and accumulates each CTA's 128
+//     rows in its own TMEM; commits arrive on both CTAs' barriers (tcgen05.commit multicast);
+//   * every TMA load completes its bytes on the leader's barrier (the .cta_group::2 form of the
+//     tensor load, no multicast); each CTA's epilogue reads its own TMEM and releases the
+//     accumulator on the leader's barrier.
+// Roles per CTA: warp 0 TMA producer, warp 1 TMEM allocation (collective for the pair) and, in the
+// leader, the MMA issuer; warps 2-5 epilogue. Two 256-column accumulators double-buffer the
+// epilogue against the next tile's MMAs. Every mbarrier wait is bounded. Results are bitwise equal
+// to the single-CTA kernel's (same K order per output element).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <atomic>
+
+#include "g16_internal.cuh"
+#include "g16_ptx.cuh"
+
+namespace g16 {
+namespace {
+
+constexpr int kPrThreads = 192;
+constexpr int kPrEpiWarps = 4;
+constexpr int kPrStages = 6;
+constexpr uint32_t kPrABytes = kBM * kBK * 2;       // this CTA's 128 rows x 64 k: 16 KiB
+constexpr uint32_t kPrBBoxBytes = kBK * 64 * 2;     // [64 k x 64 n]: 8 KiB
+constexpr uint32_t kPrBBytes = 2 * kPrBBoxBytes;    // this CTA's 128-column half of B
+constexpr uint32_t kPrStageBytes = kPrABytes + kPrBBytes;  // 32 KiB per CTA
+constexpr uint32_t kPrTmemCols = 2 * kBN;           // two 256-column accumulators
+constexpr int kPrGroupM = 8;                        // rasterisation: 8 pair-rows (2048 rows) per group
+constexpr size_t kPrSmemBytes = 1024 + kPrStages * kPrStageBytes + 256;
+static_assert(kPrSmemBytes <= 227 * 1024, "pair GEMM shared memory");
+
+struct PairArgs {
+  void* out;
+  const float* bias;
+  const float* rscale;
+  int* status;
+  int M, N, K;
+  int m2_tiles, n_tiles, units, kblocks;  // tiles of 256 x 256
+};
+
+__device__ __forceinline__ void pair_coords(const PairArgs& a, int u, int* mt2, int* nt) {
+  const int per_group = kPrGroupM * a.n_tiles;
+  const int g = u / per_group;
+  const int first = g * kPrGroupM;
+  const int gsize = min(kPrGroupM, a.m2_tiles - first);
+  const int in_g = u - g * per_group;
+  *mt2 = first + in_g % gsize;
+  *nt = in_g / gsize;
+}
+
+template <bool OUT_F16>
+__device__ __forceinline__ void pair_store_row32(const PairArgs& a, int row, int col0, float rs, const uint32_t (&r)[32]) {
+  if (row >= a.M) return;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int col = col0 + 8 * g;
+    if (col >= a.N) break;  // N % 8 == 0
+    float o[8];
+    if (a.bias != nullptr) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.bias + col));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.bias + col + 4));
+      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = fmaf(__uint_as_float(r[8 * g + j]), rs, bb[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = __uint_as_float(r[8 * g + j]) * rs;
+    }
+    const size_t off = static_cast<size_t>(row) * a.N + col;
+    if constexpr (OUT_F16) {
+      __half2 h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) + off) = *reinterpret_cast<const uint4*>(h);
+    } else {
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + off);
+      dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+    }
+  }
+}
+
+// grid = 2 * pairs CTAs, clusters of 2 along x: CTA 2p + q is rank q of pair p.
+template <bool OUT_F16>
+__global__ void __launch_bounds__(kPrThreads, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                 const PairArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* ring = smem;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kPrStages * kPrStageBytes);
+  uint64_t* empty_bar = full_bar + kPrStages;
+  uint64_t* tfull_bar = empty_bar + kPrStages;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Uniform over the grid: every CTA returns before any barrier, cluster barrier or allocation.
+  if (static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) >
+      dynamic_smem_bytes()) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(args.status, G16_ERR_ARG);
+    return;
+  }
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t q = cluster_ctarank();  // rank in the pair (cluster of 2)
+  const bool leader = q == 0;
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+  constexpr uint16_t kPairMask = 0x3;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPrStages; ++s) {
+      mbar_init(&full_bar[s], 1);   // the leader's producer arrives (expecting both CTAs' bytes)
+      mbar_init(&empty_bar[s], 1);  // the leader's MMA commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 2 * kPrEpiWarps);  // both CTAs' epilogue warps (the leader's is used)
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kPrTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barrier initialisation and the pair's TMEM allocation, visible to both CTAs
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_phase = 0;
+      bool ok = true;
+      for (int u = pair; u < args.units && ok; u += pairs) {
+        int mt2, nt;
+        pair_coords(args, u, &mt2, &nt);
+        for (int kb = 0; kb < args.kblocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (leader) {
+            mbar_arrive_expect_tx(&full_bar[stage], 2 * kPrStageBytes);
+            armed |= 1u << stage;
+            armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+          }
+          const uint32_t bar = map_cluster(smem_u32(&full_bar[stage]), 0);
+          uint8_t* sa = ring + stage * kPrStageBytes;
+          uint8_t* sb = sa + kPrABytes;
+          tma_load_2d_pair(sa, &tmap_a, bar, kb * kBK, mt2 * 2 * kBM + static_cast<int>(q) * kBM);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            tma_load_2d_pair(sb + j * kPrBBoxBytes, &tmap_b, bar, nt * kBN + static_cast<int>(q) * (kBN / 2) + 64 * j,
+                             kb * kBK);
+          if (++stage == kPrStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(args.status, G16_ERR_TIMEOUT);
+        // The leader's full barriers count both CTAs' bytes: wait for every armed stage, so no
+        // copy is still landing when the pair passes its final cluster barrier.
+        for (int s = 0; s < kPrStages; ++s)
+          if ((armed >> s) & 1u) mbar_wait(&full_bar[s], (armed_phase >> s) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA) ----------------
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_f16_f32(2 * kBM, kBN, /*b_mn_major=*/true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = pair; u < args.units && ok; u += pairs) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * kBN);
+        for (int kb = 0; kb < args.kblocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(ring + stage * kPrStageBytes);
+          const uint32_t sb = sa + kPrABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // A: K-major, 128-byte rows, 8-row atoms 1024 B apart (SBO); K steps of 32 B.
+            const uint64_t adesc = smem_desc_sw128(sa + k * (kUmmaK * 2), 16, 1024);
+            // B: N-major, the two 64-column boxes 8 KiB apart (LBO), 8-row k groups 1024 B (SBO).
+            const uint64_t bdesc = smem_desc_sw128(sb + k * (kUmmaK * 128), kPrBBoxBytes, 1024);
+            umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty_bar[stage], kPairMask);
+          if (++stage == kPrStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull_bar[acc], kPairMask);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(args.status, G16_ERR_TIMEOUT);
+      }
+      umma_commit_pair(drain_bar, kPairMask);  // every issued MMA complete, in both CTAs
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int quarter = warp & 3;
+    const int r_local = quarter * 32 + lane;
+    const uint32_t tempty_leader[2] = {map_cluster(smem_u32(&tempty_bar[0]), 0),
+                                       map_cluster(smem_u32(&tempty_bar[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = pair; u < args.units; u += pairs) {
+      int mt2, nt;
+      pair_coords(args, u, &mt2, &nt);
+      bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag);
+      got = __all_sync(0xffffffffu, got);
+      if (!got) {
+        if (lane == 0) {
+          *abort_flag = 1;
+          atomicExch(args.status, G16_ERR_TIMEOUT);
+        }
+        break;
+      }
+      tc_fence_after();
+      const int row = mt2 * 2 * kBM + static_cast<int>(q) * kBM + r_local;
+      const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        pair_store_row32<OUT_F16>(args, row, nt * kBN + c * 32, rs, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  // TMEM is released only after every MMA of the pair has completed and both CTAs are done.
+  if (warp == 1) {
+    if (lane == 0) mbar_wait(drain_bar, 0, nullptr);
+    __syncwarp();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem, kPrTmemCols);
+  }
+}
+
+template <typename F>
+cudaError_t ensure_pair_attr(F* kern, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kPrSmemBytes));
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+std::atomic<uint64_t> g_pair_attr16{0}, g_pair_attr32{0};
+
+}  // namespace
+
+// Whether a cluster of two pair-GEMM CTAs can be resident on the current device (cached).
+bool gemm_pair_available() {
+  static std::atomic<uint64_t> known{0}, ok{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (known.load(std::memory_order_acquire) & bit) return (ok.load(std::memory_order_acquire) & bit) != 0;
+  bool good = ensure_pair_attr(gemm_pair_kernel<true>, g_pair_attr16) == cudaSuccess &&
+              ensure_pair_attr(gemm_pair_kernel<false>, g_pair_attr32) == cudaSuccess;
+  if (good) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kPrThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPrSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int active = 0;
+    good = cudaOccupancyMaxActiveClusters(&active, gemm_pair_kernel<true>, &cfg) == cudaSuccess && active >= 1;
+    (void)cudaGetLastError();
+  }
+  if (good) ok.fetch_or(bit, std::memory_order_acq_rel);
+  known.fetch_or(bit, std::memory_order_acq_rel);
+  return good;
+}
+
+int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev) {
+  if (M <= 0 || N <= 0) return G16_OK;
+  PairArgs args{};
+  args.out = out;
+  args.bias = bias;
+  args.rscale = rscale;
+  args.status = device_status_ptr();
+  if (args.status == nullptr) return G16_ERR_CUDA;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.m2_tiles = (M + 2 * kBM - 1) / (2 * kBM);
+  args.n_tiles = (N + kBN - 1) / kBN;
+  args.units = args.m2_tiles * args.n_tiles;
+  args.kblocks = (K + kBK - 1) / kBK;
+  if (args.kblocks < 1) return G16_ERR_ARG;
+  CUtensorMap ta, tb;
+  int st = make_tmap_2d(&ta, a16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(M),
+                        static_cast<uint64_t>(K), kBM, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != G16_OK) return st;
+  st = make_tmap_2d(&tb, b16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                    kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != G16_OK) return st;
+  const int max_pairs = dev.sm_count / 2;
+  const int pairs = args.units < max_pairs ? args.units : max_pairs;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kPrThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPrSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+  if (out_dtype == G16_F16) {
+    e = ensure_pair_attr(gemm_pair_kernel<true>, g_pair_attr16);
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<true>, ta, tb, args);
+  } else {
+    e = ensure_pair_attr(gemm_pair_kernel<false>, g_pair_attr32);
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, args);
+  }
+  if (e != cudaSuccess) return cuda_fail(e);
+  note_launch();
+  return G16_OK;
+}
+
+}  // namespace g16

@@ -55,6 +55,11 @@ int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* d
                         int flags, cudaStream_t s, const DeviceInfo& dev);
 int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
 
+// GEMM on CTA pairs (g16_gemm_pair.cu): persistent, 256 x 256 tiles, tcgen05.mma.cta_group::2.
+int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev);
+bool gemm_pair_available();
+
 // Small-problem GEMM (g16_gemm_small.cu): one CTA per (tile, K chunk), K chunks of a tile reduced
 // inside a thread-block cluster. bn = 0: the problem has enough tiles for the persistent kernel.
 struct SmallPlan {

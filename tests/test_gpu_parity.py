@@ -241,12 +241,14 @@ def test_automatic_small_problem_plan(cuda_ok, M, K, N, out_dtype):
         assert ((y.double() - ref).norm() / ref.norm()).item() < GEMM_NORM, what
 
 
-@pytest.mark.parametrize("M,K,N", [(4096, 1024, 4096), (2048, 512, 5120), (1000, 520, 5000)])
+@pytest.mark.parametrize("M,K,N", [(4096, 1024, 4096), (2048, 512, 5120), (1000, 520, 5000), (512, 256, 12288),
+                                   (1000, 776, 12296)])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
-def test_persistent_gemm_split_tail(cuda_ok, M, K, N, out_dtype):
-    """Outputs whose last partial wave of 128 x 256 tiles fits in half the SMs: those tiles run as
-    128-column halves (512 tiles on 148 SMs: the last 68 as 136 halves). Deterministic, within the
-    GEMM tolerance, bias on every column including the ragged last tile."""
+def test_persistent_gemm_single_pass(cuda_ok, M, K, N, out_dtype):
+    """Single-pass GEMMs: N <= 8192 on CTA pairs (256 x 256 tiles), wider outputs on the single-CTA
+    kernel, whose last partial wave runs as 128-column halves when it fits in half the SMs (512 x
+    12288: 192 tiles on 148 SMs, the last 44 as 88 halves). Deterministic, within the GEMM
+    tolerance, bias on every column including ragged last tiles."""
     gen = torch.Generator(device="cuda").manual_seed(M + K + N)
     a = torch.randn(M, K, device="cuda", generator=gen).half()
     b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
