@@ -245,10 +245,12 @@ def test_automatic_small_problem_plan(cuda_ok, M, K, N, out_dtype):
                                    (1000, 776, 12296)])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 def test_persistent_gemm_single_pass(cuda_ok, M, K, N, out_dtype):
-    """Single-pass GEMMs: N <= 8192 on CTA pairs (256 x 256 tiles), wider outputs on the single-CTA
-    kernel, whose last partial wave runs as 128-column halves when it fits in half the SMs (512 x
-    12288: 192 tiles on 148 SMs, the last 44 as 88 halves). Deterministic, within the GEMM
-    tolerance, bias on every column including ragged last tiles."""
+    """Explicit single-pass GEMMs (ksplit = 1): N <= 8192 on CTA pairs (256 x 256 tiles), every tile
+    over the whole K; wider outputs on the single-CTA kernel, whose last partial wave runs as
+    128-column halves when it fits in half the SMs (512 x 12288: 192 tiles on 148 SMs, the last 44
+    as 88 halves). Deterministic, bitwise equal to the single-CTA kernel (reached through the
+    one-destination scatter entry point), within the GEMM tolerance, bias on every column including
+    ragged last tiles."""
     gen = torch.Generator(device="cuda").manual_seed(M + K + N)
     a = torch.randn(M, K, device="cuda", generator=gen).half()
     b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
@@ -256,7 +258,84 @@ def test_persistent_gemm_single_pass(cuda_ok, M, K, N, out_dtype):
     y0 = _gemm_c(a, b, bias, None, out_dtype, 1)
     y1 = _gemm_c(a, b, bias, None, out_dtype, 1)
     assert torch.equal(y0, y1)
+    single = torch.empty_like(y0)
+    ptrs = (ctypes.c_void_p * 1)(single.data_ptr())
+    st = _native.lib().g16_gemm_scatter(a.data_ptr(), b.data_ptr(), ptrs, 1, _native.dtype_code(out_dtype),
+                                        bias.data_ptr(), None, M, K, N, N, 0, 0, _native.stream_handle(0))
+    _native.check(st, "g16_gemm_scatter")
+    assert torch.equal(y0, single)
     assert_close_fp64(y0, a, b, bias, out_dtype, "split tail")
+
+
+# (M, K, N): pair tiles, tiles left after the full waves on 74 pairs (T), contributors per tail tile
+PAIR_TAIL_CASES = [(4096, 4096, 4096),   # 256 tiles, T = 34, 2 K ranges of 32 blocks
+                   (2048, 4096, 5120),   # 160 tiles, T = 12, 4 K ranges of 16 blocks
+                   (2048, 3072, 3072),   # 96 tiles, T = 22, 3 K ranges of 16 blocks
+                   (1000, 2056, 5000)]   # 80 tiles, T = 6, 2 K ranges (17 + 16 blocks), ragged M, N, K
+
+
+@pytest.mark.parametrize("M,K,N", PAIR_TAIL_CASES)
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_pair_gemm_k_split_tail(cuda_ok, M, K, N, out_dtype):
+    """Automatic plan (ksplit = 0) on the pair kernel: the last partial wave's tiles run as 2-4 K
+    ranges on otherwise idle pairs; the last contributor to arrive adds the fp32 partials in K order.
+    The workspace query covers the partials; results are deterministic (same bits on every call,
+    whichever contributor finishes last), within the GEMM tolerance of fp64 with bias and per-row
+    unscale; without a workspace the same call runs every tile as a single pass and equals ksplit = 1
+    bit for bit."""
+    L = _native.lib()
+    assert int(L.g16_gemm_workspace_bytes(M, K, N, 0)) > 0
+    gen = torch.Generator(device="cuda").manual_seed(M + K + N)
+    a = torch.randn(M, K, device="cuda", generator=gen).half()
+    b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
+    bias = torch.randn(N, device="cuda", generator=gen)
+    rscale = torch.where(torch.rand(M, device="cuda", generator=gen) < 0.1, 4.0, 1.0)
+    y0 = _gemm_c(a, b, bias, rscale, out_dtype, 0)
+    for _ in range(3):
+        assert torch.equal(_gemm_c(a, b, bias, rscale, out_dtype, 0), y0)
+    ref = (a.double() @ b.double()) * rscale.double()[:, None] + bias.double()
+    assert torch.isfinite(y0).all()
+    assert ((y0.double() - ref).norm() / ref.norm()).item() < GEMM_NORM
+    single = _gemm_c(a, b, bias, rscale, out_dtype, 1)
+    assert ((single.double() - ref).norm() / ref.norm()).item() < GEMM_NORM
+    no_ws = torch.empty(M, N, device="cuda", dtype=out_dtype)
+    st = L.g16_gemm(a.data_ptr(), b.data_ptr(), no_ws.data_ptr(), _native.dtype_code(out_dtype), bias.data_ptr(),
+                    rscale.data_ptr(), M, K, N, 0, None, 0, _native.stream_handle(0))
+    assert st == 0, _native.strerror(st)
+    assert torch.equal(no_ws, single)
+    assert _native.device_status(clear=False) == _native.OK
+
+
+def test_pair_gemm_k_split_tail_in_cuda_graph(cuda_ok):
+    """The tail's arrival counters are zeroed by a memset node before each launch, so replays of a
+    captured graph (same workspace, same arguments) stay correct and identical to eager calls."""
+    L = _native.lib()
+    M = K = N = 4096
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    a = torch.randn(M, K, device="cuda", generator=gen).half()
+    b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
+    nws = int(L.g16_gemm_workspace_bytes(M, K, N, 0))
+    ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
+    out = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        def call():
+            st = L.g16_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), _native.G16_F16, None, None, M, K, N, 0,
+                            ws.data_ptr(), nws, side.cuda_stream)
+            assert st == 0, _native.strerror(st)
+        call()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            call()
+    torch.cuda.current_stream().wait_stream(side)
+    for rep in range(3):
+        a.copy_(torch.randn(M, K, device="cuda", generator=gen).half())
+        graph.replay()
+        torch.cuda.synchronize()
+        eager = _gemm_c(a, b, None, None, torch.float16, 0)
+        assert torch.equal(out, eager), rep
+    del graph
 
 
 def test_rowscale_through_c_abi(cuda_ok):
