@@ -7,6 +7,8 @@ Workloads (a "step" is one call of the hot path on one batch o
   skinny     mm_t M=8, K=N=4096, fp32 x, fp16 w_t, fp32 bias/out (config 2)
   splitk     mm_t 128x16384x1024 fp16 -> fp16 (config 3, split-K shape)
   rescale    mm_t 2048x3072x1024 fp32 x with 1% rows x [100,200] (config 4)
+  decode16   16 FastLinear(4096, 4096) layers at M=1 per step, replayed from a CUDA graph
+             (gtx16_fp16.graphs); decode16_eager calls the same layers from Python
 Multi-GPU (--gpus N under torchrun): every listed workload runs as N independent replicas (the path
 has no exchange step for these shapes; scaling "weak"), value = sum over ranks (max-over-ranks time).
 
@@ -353,6 +355,80 @@ class ShardedGemm(Workload):
             f"fp32 torch.matmul {rows}x{self.K}x{b.shape[1]} (a block of the workload)"
 
 
+class Decode(Workload):
+    """Token-by-token decode through FastLinear: x [1, 4096] fp32 through 16 FastLinear(4096, 4096)
+    layers per step (BASELINE config 2's skinny shape, the reference's batch-1 usage measured by
+    its bench/overhead.py). graphed: the step is captured once with gtx16_fp16.graphs.capture and
+    replayed (input copy, one graph launch, output clone per step); eager: the 16 layers are
+    called from Python each step, host cost included. The 16 weights (512 MiB) exceed L2, so every
+    step streams them from HBM."""
+    bound = "hbm"
+    graphable = False  # the graphed variant replays its own graph; the eager one measures Python
+
+    def __init__(self, dev, graphed, layers=16, K=4096, M=1):
+        super().__init__(dev)
+        import torch.nn as nn
+
+        import gtx16_fp16 as g16
+        self.graphed, self.layers, self.K, self.M = graphed, layers, K, M
+        self.name = "decode16" if graphed else "decode16_eager"
+        self.metric = (f"FastLinear decode step HBM GB/s ({layers} x {K}x{K} layers, M={M}, "
+                       f"{'CUDA graph via gtx16_fp16.graphs' if graphed else 'eager Python calls'})")
+        self.unit = "GB/s"
+        g = torch.Generator(device=dev).manual_seed(0)
+        mods = []
+        for _ in range(layers):
+            fl = g16.FastLinear(K, K, bias=True, device=dev)
+            with torch.no_grad():
+                fl.weight_t.copy_((torch.randn(K, K, device=dev, generator=g) * 0.02).half())
+                fl.bias.copy_(torch.randn(K, device=dev, generator=g) * 0.01)
+            mods.append(fl)
+        self.model = nn.Sequential(*mods).eval()
+        self.x = torch.randn(M, K, device=dev, generator=g)
+        self.graph_step = g16.graphs.capture(self.model, self.x) if graphed else None
+
+    def config(self):
+        return {"workload": self.name, "layers": self.layers, "M": self.M, "K": self.K, "N": self.K,
+                "in": "fp32", "w": "fp16", "out": "fp32", "mode": "graph replay" if self.graphed else "eager",
+                "l2": f"{self.layers} weights = {self.layers * self.K * self.K * 2 >> 20} MiB > 126 MB L2"}
+
+    def alg_bytes(self):
+        per = 2 * self.K * self.K + 4 * self.M * self.K + 4 * self.K + 4 * self.M * self.K
+        return float(self.layers * per)
+
+    def flops(self):
+        return 2.0 * self.layers * self.M * self.K * self.K
+
+    def step(self, g16):
+        with torch.no_grad():
+            return self.graph_step(self.x) if self.graphed else self.model(self.x)
+
+    def host_inputs(self):
+        return [self.x.cpu().pin_memory()]
+
+    def host_out(self):
+        return torch.empty(self.M, self.K, dtype=torch.float32).pin_memory()
+
+    def e2e_step(self, g16, hin, hout):
+        x = hin[0].to(self.dev, non_blocking=True)
+        with torch.no_grad():
+            y = self.graph_step(x) if self.graphed else self.model(x)
+        hout.copy_(y, non_blocking=True)
+
+    def cpu_sample(self):
+        from oracle import cpu_path
+        ws = [m.weight_t.cpu() for m in self.model[:4]]
+        bs = [m.bias.cpu() for m in self.model[:4]]
+        x = self.x.cpu()
+
+        def run():
+            y = x
+            for w, b in zip(ws, bs):
+                y = cpu_path.mm_t_fp32(y, w, b)
+            return y
+        return run, 2.0 * 4 * self.M * self.K * self.K, "fp32 F.linear through 4 of the 16 layers (reference linear.py fallback)"
+
+
 class Bert(Workload):
     """BERT-base encoder inference with every Linear patched to FastLinear:
     random init (seed 0), fp32 activations, 256 sequences x 256 tokens, ids uniform in
@@ -461,6 +537,8 @@ WORKLOADS = {
     "rescale": lambda dev, w, r: MmT(dev, 2048, 3072, 1024, "rescale", torch.float32, torch.float32, 0.02, 0.0,
                                      rescale=True),
     "bert": lambda dev, w, r: Bert(dev, w, r),
+    "decode16": lambda dev, w, r: Decode(dev, True),
+    "decode16_eager": lambda dev, w, r: Decode(dev, False),
 }
 
 
@@ -707,7 +785,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="gemm4096", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--extra", default="skinny1,skinny4,skinny,splitk,splitk64,rescale",
+    ap.add_argument("--extra", default="skinny1,skinny4,skinny,splitk,splitk64,rescale,decode16,decode16_eager",
                     help="comma list of other workloads measured briefly into 'sub' (rank 0); '' to skip")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graph", type=int, default=1, help="1: time a CUDA graph of the K steps (default); 0: eager")

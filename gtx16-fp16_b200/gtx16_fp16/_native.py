@@ -108,9 +108,11 @@ def stream_handle(device_index: int) -> int:
 # ---------------------------------------------------------------------------------------------
 # Workspace: one buffer per (device, stream), grown on demand. It holds split-K partial tiles and the
 # fp16 copy of fp32 activations; no initial contents are needed. Calls on the same stream are
-# ordered, so sharing it across calls is safe.
+# ordered, so sharing it across calls is safe. A buffer that is outgrown is retired, not freed: a
+# CUDA graph captured earlier on that stream still holds its address and writes it on replay.
 # ---------------------------------------------------------------------------------------------
 _ws: dict[tuple[int, int], torch.Tensor] = {}
+_ws_retired: list[torch.Tensor] = []
 _ws_lock = threading.Lock()
 
 
@@ -125,6 +127,8 @@ def workspace(device: torch.device, stream: int, nbytes: int) -> tuple[int, int]
             buf = _ws.get(key)
             if buf is None or buf.numel() < nbytes:
                 size = max(nbytes, 0 if buf is None else 2 * buf.numel())
+                if buf is not None:
+                    _ws_retired.append(buf)
                 buf = torch.empty(size, dtype=torch.uint8, device=device)
                 _ws[key] = buf
     return buf.data_ptr(), buf.numel()
