@@ -331,6 +331,13 @@ int g16_gemm_plan(int M, int K, int N, int* info) {
   int st = G16_OK;
   const DeviceInfo* dev = device_info(&st);
   if (dev == nullptr) return st;
+  const int ranks = gemm_midm_ranks(M, K, N, *dev);
+  if (ranks > 0) {
+    info[0] = 2;
+    info[1] = 128;
+    info[2] = ranks;
+    return G16_OK;
+  }
   const SmallPlan p = plan_gemm_small(M, K, N, *dev);
   info[0] = p.bn != 0 ? 1 : 0;
   info[1] = p.bn != 0 ? p.bn : kBN;

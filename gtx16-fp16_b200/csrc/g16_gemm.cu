@@ -31,6 +31,10 @@
 #include "g16_internal.cuh"
 #include "g16_ptx.cuh"
 
+#ifndef G16_MIDM_DISPATCH
+#define G16_MIDM_DISPATCH 1
+#endif
+
 namespace g16 {
 namespace {
 
@@ -578,6 +582,11 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
                 const DeviceInfo& dev) {
   if (M <= 0 || N <= 0) return G16_OK;
   const int kblocks = (K + kBK - 1) / kBK;
+  // Automatic plan, M <= 64: the swapped-operand kernel (weight columns as the MMA's M).
+  if (ksplit == 0 && M <= kMidMaxM && G16_MIDM_DISPATCH) {
+    const int st = launch_gemm_midm(a16, b16, out, out_dtype, bias, rscale, M, K, N, s, dev);
+    if (st != G16_ERR_UNSUPPORTED) return st;
+  }
   if (ksplit == 0) {
     const SmallPlan p = plan_gemm_small(M, K, N, dev);
     if (p.bn != 0) {

@@ -60,6 +60,14 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
                      const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev);
 bool gemm_pair_available();
 
+// Medium-M GEMM (g16_gemm_midm.cu): M <= kMidMaxM activation rows, operands swapped so the
+// weight columns are the MMA's M and the rows its N; K split over a cluster, reduced in DSMEM.
+constexpr int kMidMaxM = 64;
+int launch_gemm_midm(const uint16_t* x16, const uint16_t* w, void* out, int out_dtype, const float* bias,
+                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev);
+// Cluster size (K ranks) of the medium-M plan for this shape, 0 when it does not apply.
+int gemm_midm_ranks(int M, int K, int N, const DeviceInfo& dev);
+
 // Small-problem GEMM (g16_gemm_small.cu): one CTA per (tile, K chunk), K chunks of a tile reduced
 // inside a thread-block cluster. bn = 0: the problem has enough tiles for the persistent kernel.
 struct SmallPlan {

@@ -86,9 +86,11 @@ int g16_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M
  * Tensor-core GEMM: out[M,N] = (a16[M,K] @ b16[K,N]) * rscale[row] + bias[col], fp32 accumulate in
  * TMEM, fused epilogue. Replaces hgemm_f32out / hgemm_f16out / hgemm_splitk
  * (src/gtx16_fp16/kernels.py:139-151). rscale and bias may be NULL. ksplit = 0 picks the plan
- * automatically: when the output has too few 128 x 256 tiles to fill the GPU, a kernel with one
- * CTA per (tile, K chunk), 128- or 256-wide tiles and the K chunks of a tile reduced inside a
- * thread-block cluster (no workspace used); otherwise the persistent kernel. ksplit = 1 forces a
+ * automatically: for M <= 64 a kernel with the operands swapped (128 weight columns per CTA as
+ * the MMA's M, the rows as its N, K split over a cluster and reduced in shared memory); else,
+ * when the output has too few 128 x 256 tiles to fill the GPU, a kernel with one CTA per (tile,
+ * K chunk), 128- or 256-wide tiles and the K chunks of a tile reduced inside a thread-block
+ * cluster (no workspace used); otherwise the persistent kernels. ksplit = 1 forces a
  * single pass; ksplit > 1 forces that many K chunks: 2..16 are reduced in a cluster when one can
  * be resident, else (and for ksplit > 16) through the workspace, which must hold
  * g16_gemm_workspace_bytes(M,K,N,ksplit). Both reductions add the chunks' fp32 partials in chunk
@@ -165,10 +167,11 @@ int g16_ipc_open(const void* handle, void** ptr);
 int g16_ipc_close(void* ptr);
 
 /* Plan g16_gemm uses for ksplit = 0 on the current device (introspection for tests and tuning; no
- * counterpart in the reference, whose choice is the split-K rule of ops.py:92-101): info[0] = 1 the
- * small-problem kernel (one CTA per tile and K chunk) / 0 the persistent kernel, [1] tile width N
- * (128 or 256), [2] K chunks (cluster size; for the persistent kernel the workspace split).
- * info must hold 3 ints. */
+ * counterpart in the reference, whose choice is the split-K rule of ops.py:92-101): info[0] = 2 the
+ * medium-M kernel (M <= 64: weight columns as the MMA's M, 128-column strips) / 1 the
+ * small-problem kernel (one CTA per tile and K chunk) / 0 the persistent kernels, [1] tile width
+ * (128 or 256; the strip width for kind 2), [2] K chunks (cluster size; for the persistent kernel
+ * the workspace split). info must hold 3 ints. */
 int g16_gemm_plan(int M, int K, int N, int* info);
 
 /* Device-side status word of the current device: G16_OK, or G16_ERR_TIMEOUT if a kernel's

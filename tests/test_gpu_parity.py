@@ -17,7 +17,8 @@ pytestmark = pytest.mark.gpu
 SHAPES = [  # (M, K, N): tile-aligned, ragged edges, skinny (M <= 8), tiny (tests/test_correctness.py:14-18)
     (128, 128, 128), (256, 512, 384), (1000, 1032, 776), (129, 136, 8), (3, 4096, 4096),
     (1, 1024, 3072), (8, 2048, 520), (9, 64, 64), (4096, 4096, 1024), (17, 8, 4104),
-    (64, 1024, 1024), (33, 4096, 768), (200, 1032, 136),  # split-K path
+    (64, 1024, 1024), (33, 4096, 768),  # medium-M path (M <= 64, swapped operands)
+    (200, 1032, 136),  # split-K path
 ]
 
 
@@ -267,75 +268,58 @@ def test_persistent_gemm_single_pass(cuda_ok, M, K, N, out_dtype):
     assert_close_fp64(y0, a, b, bias, out_dtype, "split tail")
 
 
-# (M, K, N): pair tiles, tiles left after the full waves on 74 pairs (T), contributors per tail tile
-PAIR_TAIL_CASES = [(4096, 4096, 4096),   # 256 tiles, T = 34, 2 K ranges of 32 blocks
-                   (2048, 4096, 5120),   # 160 tiles, T = 12, 4 K ranges of 16 blocks
-                   (2048, 3072, 3072),   # 96 tiles, T = 22, 3 K ranges of 16 blocks
-                   (1000, 2056, 5000)]   # 80 tiles, T = 6, 2 K ranges (17 + 16 blocks), ragged M, N, K
+MEDIUM_M = [(1, 1024, 768), (9, 64, 64), (16, 4096, 4096), (17, 1032, 776), (32, 768, 3072), (33, 4096, 768),
+            (48, 16384, 1024), (64, 1024, 1024), (64, 520, 4104), (40, 8, 136)]
 
 
-@pytest.mark.parametrize("M,K,N", PAIR_TAIL_CASES)
-@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
-def test_pair_gemm_k_split_tail(cuda_ok, M, K, N, out_dtype):
-    """Automatic plan (ksplit = 0) on the pair kernel: the last partial wave's tiles run as 2-4 K
-    ranges on otherwise idle pairs; the last contributor to arrive adds the fp32 partials in K order.
-    The workspace query covers the partials; results are deterministic (same bits on every call,
-    whichever contributor finishes last), within the GEMM tolerance of fp64 with bias and per-row
-    unscale; without a workspace the same call runs every tile as a single pass and equals ksplit = 1
-    bit for bit."""
+@pytest.mark.parametrize("M,K,N", MEDIUM_M)
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+def test_medium_m_kernel(cuda_ok, M, K, N, out_dtype):
+    """Automatic plan for M <= 64: the swapped-operand kernel (128 weight columns per CTA as the
+    MMA's M, the rows as its N padded to 16/32/64, K split over a cluster and the partials added in
+    rank order). Reported by g16_gemm_plan; deterministic; within the GEMM tolerance of fp64 with
+    bias and per-row unscale, ragged M, N and K (K = 8 and K = 520 leave a partial 64-wide step)."""
     L = _native.lib()
-    assert int(L.g16_gemm_workspace_bytes(M, K, N, 0)) > 0
-    gen = torch.Generator(device="cuda").manual_seed(M + K + N)
+    info = (ctypes.c_int * 3)()
+    assert L.g16_gemm_plan(M, K, N, info) == 0
+    assert info[0] == 2 and info[1] == 128 and info[2] >= 1
+    gen = torch.Generator(device="cuda").manual_seed(M * 31 + K + N)
     a = torch.randn(M, K, device="cuda", generator=gen).half()
     b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
     bias = torch.randn(N, device="cuda", generator=gen)
-    rscale = torch.where(torch.rand(M, device="cuda", generator=gen) < 0.1, 4.0, 1.0)
+    rscale = torch.where(torch.rand(M, device="cuda", generator=gen) < 0.25, 8.0, 1.0)
     y0 = _gemm_c(a, b, bias, rscale, out_dtype, 0)
-    for _ in range(3):
-        assert torch.equal(_gemm_c(a, b, bias, rscale, out_dtype, 0), y0)
+    y1 = _gemm_c(a, b, bias, rscale, out_dtype, 0)
+    assert torch.equal(y0, y1)
     ref = (a.double() @ b.double()) * rscale.double()[:, None] + bias.double()
     assert torch.isfinite(y0).all()
     assert ((y0.double() - ref).norm() / ref.norm()).item() < GEMM_NORM
-    single = _gemm_c(a, b, bias, rscale, out_dtype, 1)
-    assert ((single.double() - ref).norm() / ref.norm()).item() < GEMM_NORM
-    no_ws = torch.empty(M, N, device="cuda", dtype=out_dtype)
-    st = L.g16_gemm(a.data_ptr(), b.data_ptr(), no_ws.data_ptr(), _native.dtype_code(out_dtype), bias.data_ptr(),
-                    rscale.data_ptr(), M, K, N, 0, None, 0, _native.stream_handle(0))
-    assert st == 0, _native.strerror(st)
-    assert torch.equal(no_ws, single)
-    assert _native.device_status(clear=False) == _native.OK
+    single = _gemm_c(a, b, bias, rscale, out_dtype, 1)  # the 128-row-tile kernels
+    assert ((y0.double() - single.double()).norm() / ref.norm()).item() < GEMM_NORM
 
 
-def test_pair_gemm_k_split_tail_in_cuda_graph(cuda_ok):
-    """The tail's arrival counters are zeroed by a memset node before each launch, so replays of a
-    captured graph (same workspace, same arguments) stay correct and identical to eager calls."""
+def test_medium_m_plan_boundary(cuda_ok):
     L = _native.lib()
-    M = K = N = 4096
-    gen = torch.Generator(device="cuda").manual_seed(11)
-    a = torch.randn(M, K, device="cuda", generator=gen).half()
-    b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
-    nws = int(L.g16_gemm_workspace_bytes(M, K, N, 0))
-    ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
-    out = torch.empty(M, N, device="cuda", dtype=torch.float16)
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        def call():
-            st = L.g16_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), _native.G16_F16, None, None, M, K, N, 0,
-                            ws.data_ptr(), nws, side.cuda_stream)
-            assert st == 0, _native.strerror(st)
-        call()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            call()
-    torch.cuda.current_stream().wait_stream(side)
-    for rep in range(3):
-        a.copy_(torch.randn(M, K, device="cuda", generator=gen).half())
-        graph.replay()
-        torch.cuda.synchronize()
-        eager = _gemm_c(a, b, None, None, torch.float16, 0)
-        assert torch.equal(out, eager), rep
-    del graph
+    info = (ctypes.c_int * 3)()
+    assert L.g16_gemm_plan(64, 4096, 4096, info) == 0 and info[0] == 2
+    assert L.g16_gemm_plan(65, 4096, 4096, info) == 0 and info[0] != 2
+
+
+@pytest.mark.parametrize("M", [9, 24, 64])
+def test_medium_m_fp32_activations_with_rescale(cuda_ok, M):
+    """mm_t with fp32 activations, 8 < M <= 64: rowscale (rows above |1024| scaled by a power of two)
+    then the medium-M kernel with the unscale in its epilogue; a row with a 1.2e5 spike stays finite
+    and accurate."""
+    torch.manual_seed(M)
+    x = torch.randn(M, 3072, device="cuda")
+    x[M // 2, 17] = 120000.0
+    w = (torch.randn(3072, 1024, device="cuda") * 0.02).half()
+    b = torch.randn(1024, device="cuda")
+    y = g.mm_t(x, w, b, torch.float32)
+    ref = x.double() @ w.double() + b.double()
+    assert torch.isfinite(y).all()
+    assert ((y.double() - ref).norm() / ref.norm()).item() < GEMM_NORM
+    assert torch.equal(y, g.mm_t(x, w, b, torch.float32))
 
 
 def test_rowscale_through_c_abi(cuda_ok):
