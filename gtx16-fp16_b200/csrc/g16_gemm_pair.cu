@@ -12,8 +12,11 @@
 //     accumulator on the leader's barrier.
 // Roles per CTA: warp 0 TMA producer, warp 1 TMEM allocation (collective for the pair) and, in the
 // leader, the MMA issuer; warps 2-5 epilogue. Two 256-column accumulators double-buffer the
-// epilogue against the next tile's MMAs. Every mbarrier wait is bounded. Results are bitwise equal
-// to the single-CTA kernel's (same K order per output element).
+// epilogue against the next tile's MMAs. The epilogue stages each warp's 32 rows x 128 bytes
+// (32 fp32 or 64 fp16 columns) in a 128-byte-swizzled shared buffer (two per warp, alternating) and
+// writes it with a TMA tile store, so global writes are whole lines and ragged edges are clipped
+// by the tensor map. Every mbarrier wait is bounded. Results are bitwise equal to the single-CTA
+// kernel's (same K order per output element).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -35,7 +38,9 @@ constexpr uint32_t kPrBBytes = 2 * kPrBBoxBytes;    // this CTA's 128-column hal
 constexpr uint32_t kPrStageBytes = kPrABytes + kPrBBytes;  // 32 KiB per CTA
 constexpr uint32_t kPrTmemCols = 2 * kBN;           // two 256-column accumulators
 constexpr int kPrGroupM = 8;                        // rasterisation: 8 pair-rows (2048 rows) per group
-constexpr size_t kPrSmemBytes = 1024 + kPrStages * kPrStageBytes + 256;
+constexpr uint32_t kPrEpiBufBytes = 32 * 128;             // one warp's 32 rows x 128 bytes
+constexpr uint32_t kPrEpiBytes = kPrEpiWarps * 2 * kPrEpiBufBytes;  // two buffers per epilogue warp
+constexpr size_t kPrSmemBytes = 1024 + kPrStages * kPrStageBytes + kPrEpiBytes + 256;
 static_assert(kPrSmemBytes <= 227 * 1024, "pair GEMM shared memory");
 
 struct PairArgs {
@@ -57,15 +62,15 @@ __device__ __forceinline__ void pair_coords(const PairArgs& a, int u, int* mt2, 
   *nt = in_g / gsize;
 }
 
+// Epilogue math for 32 accumulator columns of one row: acc * rscale + bias, packed as 4 (fp16) or
+// 8 (fp32) 16-byte chunks of the row segment.
 template <bool OUT_F16>
-__device__ __forceinline__ void pair_store_row32(const PairArgs& a, int row, int col0, float rs, const uint32_t (&r)[32]) {
-  if (row >= a.M) return;
+__device__ __forceinline__ void pair_pack32(const PairArgs& a, int col0, float rs, const uint32_t (&r)[32], uint4* out) {
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     const int col = col0 + 8 * g;
-    if (col >= a.N) break;  // N % 8 == 0
     float o[8];
-    if (a.bias != nullptr) {
+    if (a.bias != nullptr && col < a.N) {  // N % 8 == 0: 8 columns are all in or all out
       const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.bias + col));
       const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.bias + col + 4));
       const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
@@ -75,16 +80,15 @@ __device__ __forceinline__ void pair_store_row32(const PairArgs& a, int row, int
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = __uint_as_float(r[8 * g + j]) * rs;
     }
-    const size_t off = static_cast<size_t>(row) * a.N + col;
     if constexpr (OUT_F16) {
       __half2 h[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
-      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) + off) = *reinterpret_cast<const uint4*>(h);
+      out[g] = *reinterpret_cast<const uint4*>(h);
     } else {
-      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + off);
-      dst[0] = make_float4(o[0], o[1], o[2], o[3]);
-      dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+      out[2 * g] = make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3]));
+      out[2 * g + 1] =
+          make_uint4(__float_as_uint(o[4]), __float_as_uint(o[5]), __float_as_uint(o[6]), __float_as_uint(o[7]));
     }
   }
 }
@@ -93,11 +97,13 @@ __device__ __forceinline__ void pair_store_row32(const PairArgs& a, int row, int
 template <bool OUT_F16>
 __global__ void __launch_bounds__(kPrThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                 const __grid_constant__ CUtensorMap tmap_out,
                  const PairArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* ring = smem;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kPrStages * kPrStageBytes);
+  uint8_t* epi_stage = smem + kPrStages * kPrStageBytes;  // 1024-byte aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_stage + kPrEpiBytes);
   uint64_t* empty_bar = full_bar + kPrStages;
   uint64_t* tfull_bar = empty_bar + kPrStages;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -135,6 +141,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_out);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kPrTmemCols);
@@ -232,6 +239,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
                                        map_cluster(smem_u32(&tempty_bar[1]), 0)};
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t nbuf = 0;  // staging buffers used so far by this warp (alternating)
+    uint8_t* my_stage = epi_stage + quarter * 2 * kPrEpiBufBytes;
+    constexpr int kCols = OUT_F16 ? 64 : 32;  // columns per 128-byte row segment
     for (int u = pair; u < args.units; u += pairs) {
       int mt2, nt;
       pair_coords(args, u, &mt2, &nt);
@@ -248,13 +258,31 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       const int row = mt2 * 2 * kBM + static_cast<int>(q) * kBM + r_local;
       const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+      const int y = mt2 * 2 * kBM + static_cast<int>(q) * kBM + quarter * 32;  // the warp's first row
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
+      for (int c0 = 0; c0 < kBN; c0 += kCols, ++nbuf) {
+        const int gcol = nt * kBN + c0;
+        uint4 packed[8];
+#pragma unroll
+        for (int h = 0; h < kCols / 32; ++h) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(t_row + c0 + h * 32, r);
+          tmem_ld_wait();
+          pair_pack32<OUT_F16>(args, gcol + h * 32, rs, r, packed + (OUT_F16 ? 4 : 8) * h);
+        }
+        uint8_t* buf = my_stage + (nbuf & 1u) * kPrEpiBufBytes;
+        if (lane == 0) bulk_wait_group_read1();  // the store that last read `buf` has read it
         __syncwarp();
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        pair_store_row32<OUT_F16>(args, row, nt * kBN + c * 32, rs, r);
+        // this lane's row: 8 chunks of 16 bytes, swizzled by row (the tensor map's 128-byte swizzle)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = packed[j];
+        fence_proxy_async_smem();  // staged rows -> visible to the TMA engine
+        __syncwarp();
+        if (lane == 0) {
+          if (y < args.M && gcol < args.N) tma_store_2d(&tmap_out, buf, gcol, y);
+          bulk_commit_group();
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -263,6 +291,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     }
   }
 
+  // Every tile store has completed before the grid ends.
+  if (warp >= 2 && lane == 0) bulk_wait_group0();
   // TMEM is released only after every MMA of the pair has completed and both CTAs are done.
   if (warp == 1) {
     if (lane == 0) mbar_wait(drain_bar, 0, nullptr);
@@ -347,6 +377,12 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
   st = make_tmap_2d(&tb, b16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                     kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
+  // Output: [32 rows x 128 bytes] boxes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
+  CUtensorMap to;
+  const bool f16 = out_dtype == G16_F16;
+  st = make_tmap_2d(&to, out, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, f16 ? 2 : 4,
+                    static_cast<uint64_t>(M), static_cast<uint64_t>(N), 32, f16 ? 64 : 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != G16_OK) return st;
   const int max_pairs = dev.sm_count / 2;
   const int pairs = args.units < max_pairs ? args.units : max_pairs;
   cudaLaunchConfig_t cfg{};
@@ -364,10 +400,10 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
   cudaError_t e;
   if (out_dtype == G16_F16) {
     e = ensure_pair_attr(gemm_pair_kernel<true>, g_pair_attr16);
-    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<true>, ta, tb, args);
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<true>, ta, tb, to, args);
   } else {
     e = ensure_pair_attr(gemm_pair_kernel<false>, g_pair_attr32);
-    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, args);
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, to, args);
   }
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();

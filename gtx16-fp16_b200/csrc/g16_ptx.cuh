@@ -165,6 +165,8 @@ __device__ __forceinline__ void tma_store_2d(const void* desc, const void* smem_
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // The shared-memory sources of this thread's committed groups have been read (may be rewritten).
 __device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// All but the most recent of this thread's committed groups have read their shared sources.
+__device__ __forceinline__ void bulk_wait_group_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // This thread's committed groups have completed (their writes are performed).
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
