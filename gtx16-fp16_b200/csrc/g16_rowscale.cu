@@ -9,7 +9,10 @@
 // exactly from the IEEE-754 exponent and mantissa fields of r = amax / thresh (no transcendental
 // call), so S is always the smallest power of two with amax / S <= thresh.
 //
-// One CTA per row; the row is read from HBM once (the second pass hits L1/L2) and written once.
+// Rows up to 3072 (fp32) or 4096 (fp16) elements: one warp per row, the row held in registers
+// between the |max| reduction and the scaled cast (read from HBM once, 16-byte coalesced loads,
+// a persistent grid of warps walking the rows). Longer rows: one CTA per row, the second pass
+// hitting L1/L2.
 #include <cuda_fp16.h>
 
 #include "g16_internal.cuh"
@@ -120,11 +123,115 @@ __global__ void __launch_bounds__(kThreads) rowscale_f16_kernel(const __half* __
   if (threadIdx.x == 0) S[row] = sc;
 }
 
+// Warp per row: NV 16-byte vectors per lane (row length <= 32 * NV vectors); kVec elements each.
+template <typename TX, int NV>
+__global__ void __launch_bounds__(kThreads) rowscale_warp_kernel(const TX* __restrict__ x, __half* __restrict__ y,
+                                                                 float* __restrict__ S, int M, int K, float thresh) {
+  constexpr int kVec = 16 / sizeof(TX);  // elements per 16-byte vector
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (kThreads / 32);
+  const int nvec = K / kVec;  // K % 8 == 0
+  for (int row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < M; row += warps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * K);
+    uint4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = lane + 32 * i;
+      v[i] = j < nvec ? __ldcs(xr + j) : make_uint4(0u, 0u, 0u, 0u);  // read once: evict first
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if constexpr (sizeof(TX) == 4) {
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(__uint_as_float(v[i].x)), fabsf(__uint_as_float(v[i].y))),
+                           fmaxf(fabsf(__uint_as_float(v[i].z)), fabsf(__uint_as_float(v[i].w)))));
+      } else {
+        const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(h[q]);
+          m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float inv;
+    const float sc = pow2_row_scale(m, thresh, &inv);
+    __half* yr = y + static_cast<size_t>(row) * K;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = lane + 32 * i;
+      if (j >= nvec) break;
+      if constexpr (sizeof(TX) == 4) {
+        float a = __uint_as_float(v[i].x), b = __uint_as_float(v[i].y), c = __uint_as_float(v[i].z),
+              d = __uint_as_float(v[i].w);
+        if (sc != 1.f) { a *= inv; b *= inv; c *= inv; d *= inv; }
+        const __half2 h0 = __floats2half2_rn(a, b), h1 = __floats2half2_rn(c, d);
+        uint2 o;
+        o.x = *reinterpret_cast<const uint32_t*>(&h0);
+        o.y = *reinterpret_cast<const uint32_t*>(&h1);
+        reinterpret_cast<uint2*>(yr)[j] = o;
+      } else {
+        uint4 o = v[i];
+        if (sc != 1.f) {
+          __half2* h = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(h[q]);
+            h[q] = __floats2half2_rn(f.x * inv, f.y * inv);
+          }
+        }
+        reinterpret_cast<uint4*>(yr)[j] = o;
+      }
+    }
+    if (lane == 0) S[row] = sc;
+  }
+}
+
+template <typename TX, int NV>
+cudaError_t launch_rowscale_warp(const void* x, uint16_t* y16, float* rscale, int M, int K, float thresh,
+                                 cudaStream_t s) {
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const int rows_per_block = kThreads / 32;
+  int blocks = (M + rows_per_block - 1) / rows_per_block;
+  const int cap = sms * 8;  // 64 warps per SM, each with NV loads in flight
+  if (blocks > cap) blocks = cap;
+  rowscale_warp_kernel<TX, NV><<<blocks, kThreads, 0, s>>>(static_cast<const TX*>(x), reinterpret_cast<__half*>(y16),
+                                                            rscale, M, K, thresh);
+  return cudaGetLastError();
+}
+
+template <typename TX>
+cudaError_t launch_rowscale_warp_any(const void* x, uint16_t* y16, float* rscale, int M, int K, float thresh,
+                                     cudaStream_t s) {
+  const int nvec = K / (16 / static_cast<int>(sizeof(TX)));
+  if (nvec <= 32 * 4) return launch_rowscale_warp<TX, 4>(x, y16, rscale, M, K, thresh, s);
+  if (nvec <= 32 * 8) return launch_rowscale_warp<TX, 8>(x, y16, rscale, M, K, thresh, s);
+  if constexpr (sizeof(TX) == 2) {
+    return launch_rowscale_warp<TX, 16>(x, y16, rscale, M, K, thresh, s);
+  } else {
+    if (nvec <= 32 * 16) return launch_rowscale_warp<TX, 16>(x, y16, rscale, M, K, thresh, s);
+    return launch_rowscale_warp<TX, 24>(x, y16, rscale, M, K, thresh, s);
+  }
+}
+
 }  // namespace
 
 int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M, int K, float thresh,
                     cudaStream_t s) {
   if (M <= 0) return G16_OK;
+  const int nvec = K / (x_dtype == G16_F32 ? 4 : 8);
+  if (nvec <= 32 * (x_dtype == G16_F32 ? 24 : 16)) {  // the row fits a warp's registers
+    const cudaError_t e = x_dtype == G16_F32 ? launch_rowscale_warp_any<float>(x, y16, rscale, M, K, thresh, s)
+                                             : launch_rowscale_warp_any<__half>(x, y16, rscale, M, K, thresh, s);
+    if (e != cudaSuccess) return cuda_fail(e);
+    note_launch();
+    return G16_OK;
+  }
   if (x_dtype == G16_F32) {
     rowscale_f32_kernel<<<M, kThreads, 0, s>>>(static_cast<const float*>(x), reinterpret_cast<__half*>(y16), rscale,
                                                 K, thresh);

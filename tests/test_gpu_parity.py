@@ -338,6 +338,39 @@ def test_rowscale_through_c_abi(cuda_ok):
     torch.testing.assert_close(y.float(), (x / S[:, None]).half().float(), rtol=0, atol=0)
 
 
+def _expected_row_scale(x):
+    """S = smallest power of two with amax / S <= 1024 (1 when amax <= 1024), computed exactly."""
+    amax = x.float().abs().amax(dim=1).double().cpu()
+    r = amax / 1024.0
+    m, e = torch.frexp(r)  # r = m * 2^e, m in [0.5, 1)
+    c = torch.where(m == 0.5, e - 1, e)  # ceil(log2(r))
+    return torch.where(amax > 1024.0, torch.pow(2.0, c.double()), torch.ones_like(amax)).float()
+
+
+@pytest.mark.parametrize("xdt,K", [(torch.float32, 8), (torch.float32, 768), (torch.float32, 3072),
+                                   (torch.float32, 3080), (torch.float32, 8192), (torch.float16, 4096),
+                                   (torch.float16, 4104)])
+def test_rowscale_row_lengths(cuda_ok, xdt, K):
+    """Rows that fit a warp's registers (fp32 K <= 3072, fp16 K <= 4096) and longer rows (one CTA
+    per row) give the same scale rule and the same bits as x / S cast to fp16."""
+    torch.manual_seed(K)
+    M = 300
+    x = torch.randn(M, K, device="cuda") * 4
+    x[0, K - 1] = 5000.0 if xdt == torch.float16 else 179940.0
+    x[1, 0] = -1025.0
+    x[2, K // 2] = 1024.0
+    x = x.to(xdt)
+    y = torch.empty(M, K, device="cuda", dtype=torch.float16)
+    S = torch.empty(M, device="cuda")
+    st = _native.lib().g16_rowscale(x.data_ptr(), _native.dtype_code(xdt), y.data_ptr(), S.data_ptr(), M, K, 1024.0,
+                                    _native.stream_handle(0))
+    assert st == 0
+    exp_s = _expected_row_scale(x)
+    assert torch.equal(S.cpu(), exp_s)
+    assert S[1].item() == 2.0 and S[2].item() == 1.0
+    assert torch.equal(y, (x.float() / S[:, None]).half())
+
+
 def test_k_zero_gives_bias(cuda_ok):
     x = torch.empty(16, 0, device="cuda").half()
     w = torch.empty(0, 64, device="cuda").half()
