@@ -47,6 +47,21 @@ class FastLinear(nn.Module):
     def weight(self) -> torch.Tensor:  # some model code reads .weight (e.g. for dtype/device)
         return self.weight_t.t()
 
+    def _apply(self, fn, recurse=True):
+        """Device moves apply as usual, but the storage formats the kernels read stay fixed:
+        weight_t fp16 and bias fp32, so model.half() / .float() / .to(dtype) cannot hand the kernels
+        a buffer of another type. A dtype change is dropped, not applied and undone, so no value
+        loses precision on the way."""
+        for name, want in (("weight_t", torch.float16), ("bias", torch.float32)):
+            t = self._buffers.get(name)
+            if t is None:
+                continue
+            moved = fn(t)
+            if moved.dtype != want:
+                moved = t.to(device=moved.device, dtype=want)
+            self._buffers[name] = moved
+        return self
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         out_dtype = x.dtype if x.dtype in (torch.float32, torch.float16) else torch.float32
         if torch.is_grad_enabled() and x.requires_grad:
@@ -88,14 +103,23 @@ class FastLinear(nn.Module):
 
 
 def patch(model: nn.Module, min_features: int = 256, force: bool = False,
-          skip: tuple[str, ...] = ()) -> int:
+          skip: tuple[str, ...] = (), *, activations: torch.dtype | None = None) -> int:
     """Replace nn.Linear layers in-place with FastLinear. Returns the number replaced.
 
     Same selection rules as the reference (linear.py:79-99): only on affected GPUs unless
     force=True (B200 is not "affected", so pass force=True there); CUDA weights only; in and out
     features >= min_features and multiples of 8; qualified names containing any string in `skip`
     are left alone (e.g. skip=("lm_head",) keeps an output head in fp32).
+
+    activations=torch.float16 (opt-in, not in the reference) also converts the rest of the model
+    to fp16 after the swap, so activations stay fp16 between layers: each FastLinear then reads
+    fp16 activations with no rescale pass and writes fp16, and the layers in between (attention,
+    norms, activation functions) run in torch's fp16 kernels. FastLinear keeps its own formats
+    (weight_t fp16, bias fp32). Inputs must then be fp16 (or integer ids). Accuracy follows fp16
+    activations rather than the fp32 reference semantics (linear.py:44), which is why it is opt-in.
     """
+    if activations not in (None, torch.float16, torch.float32):
+        raise ValueError(f"activations must be None, torch.float16 or torch.float32, got {activations}")
     if not force and not any(is_affected(p.device) for p in model.parameters() if p.is_cuda):
         return 0
     n = 0
@@ -108,4 +132,8 @@ def patch(model: nn.Module, min_features: int = 256, force: bool = False,
                     and not any(s in full for s in skip)):
                 setattr(mod, child_name, FastLinear.from_linear(child))
                 n += 1
+    if activations is torch.float16:
+        model.half()
+    elif activations is torch.float32:
+        model.float()
     return n

@@ -108,3 +108,26 @@ def test_state_dict_round_trip():
     assert torch.equal(fl2.weight_t, fl.weight_t) and torch.equal(fl2.bias, fl.bias)
     nb = g.FastLinear(64, 32, bias=False)
     assert nb.bias is None and "bias" not in dict(nb.named_buffers())
+
+
+def test_fast_linear_keeps_its_storage_formats_under_dtype_casts():
+    """model.half() / .float() / .double() leave weight_t fp16 and bias fp32 (the formats the kernels
+    read); the bias keeps its full fp32 value through the casts."""
+    lin = nn.Linear(64, 48)
+    with torch.no_grad():
+        lin.bias[0] = 1.0 + 2.0 ** -20  # not representable in fp16
+    m = g.FastLinear.from_linear(lin)
+    seq = nn.Sequential(m, nn.LayerNorm(48))
+    for cast in (seq.half, seq.float, seq.double, lambda: seq.to(torch.bfloat16)):
+        cast()
+        assert m.weight_t.dtype == torch.float16 and m.bias.dtype == torch.float32
+        assert m.bias[0].item() == 1.0 + 2.0 ** -20
+    seq.half()
+    assert seq[1].weight.dtype == torch.float16  # other modules do change
+    sd = m.state_dict()
+    assert sd["weight_t"].dtype == torch.float16 and sd["bias"].dtype == torch.float32
+
+
+def test_patch_rejects_unknown_activation_dtype():
+    with pytest.raises(ValueError, match="activations"):
+        g.patch(nn.Sequential(nn.Linear(8, 8)), force=True, activations=torch.bfloat16)
