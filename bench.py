@@ -438,16 +438,17 @@ class Bert(Workload):
     bound = "tensor"
     graphable = False
 
-    def __init__(self, dev, world, rank, batch=256, seq=256, reference=False, half=False):
+    def __init__(self, dev, world, rank, batch=256, seq=256, reference=False, half=False, fuse=False):
         super().__init__(dev)
         import copy
         import gtx16_fp16 as g16
         from gtx16_fp16.dist import batch_slice
         from transformers import BertConfig, BertModel
-        self.half = half
-        self.name = "bert16" if half else "bert"
-        self.metric = ("BERT-base texts/s (256 x 256 tokens, FastLinear, fp16 activations (opt-in), data parallel)"
-                       if half else "BERT-base texts/s (256 x 256 tokens, FastLinear, data parallel)")
+        self.half, self.fuse = half, fuse
+        self.name = ("bert16" if half else "bert") + ("_fused" if fuse else "")
+        opts = ", ".join(o for o, on in (("fp16 activations", half), ("GELU/QKV fused", fuse)) if on)
+        self.metric = (f"BERT-base texts/s (256 x 256 tokens, FastLinear{', ' + opts + ' (opt-in)' if opts else ''}, "
+                       "data parallel)")
         self.unit = "texts/s"
         self.scaling = "strong"
         self.world, self.rank, self.batch, self.seq = world, rank, batch, seq
@@ -461,7 +462,7 @@ class Bert(Workload):
             model = BertModel(cfg).eval()
             self.ref_model = copy.deepcopy(model).to(dev)
             self.model = model.to(dev)
-            self.n_patched = g16.patch(self.model, force=True, activations=torch.float16 if half else None)
+            self.n_patched = g16.patch(self.model, force=True, activations=torch.float16 if half else None, fuse=fuse)
         gen = torch.Generator().manual_seed(0)
         ids = torch.randint(1000, 30522, (batch, seq), generator=gen)
         sl = batch_slice(batch, world, rank)
@@ -475,6 +476,7 @@ class Bert(Workload):
         return {"workload": self.name, "model": "BERT-base (12 x 768, 12 heads, FFN 3072, random init seed 0)",
                 "global_batch": self.batch, "seq_len": self.seq, "local_batch": self.local_batch,
                 "patched_linears": self.n_patched, "activations": "fp16" if self.half else "fp32",
+                "fused": "GELU into the FFN GEMM, one QKV GEMM" if self.fuse else "none",
                 "attention": f"torch sdpa ({'fp16' if self.half else 'fp32'})",
                 "cosine_min_vs_fp32": self.cos_min, "l2": "activations 200+ MB per layer > 126 MB L2"}
 
@@ -540,7 +542,9 @@ WORKLOADS = {
     "rescale": lambda dev, w, r: MmT(dev, 2048, 3072, 1024, "rescale", torch.float32, torch.float32, 0.02, 0.0,
                                      rescale=True),
     "bert": lambda dev, w, r: Bert(dev, w, r),
+    "bert_fused": lambda dev, w, r: Bert(dev, w, r, fuse=True),
     "bert16": lambda dev, w, r: Bert(dev, w, r, half=True),
+    "bert16_fused": lambda dev, w, r: Bert(dev, w, r, half=True, fuse=True),
     "decode16": lambda dev, w, r: Decode(dev, True),
     "decode16_eager": lambda dev, w, r: Decode(dev, False),
 }
@@ -748,7 +752,7 @@ def run_reference(args, rank, world, dev):
     if rank != 0:
         return None
     from oracle import cpu_path
-    wl = (Bert(dev, 1, 0, reference=True) if args.workload in ("bert", "bert16")
+    wl = (Bert(dev, 1, 0, reference=True) if args.workload.startswith("bert")
           else WORKLOADS[args.workload](dev, 1, 0))
     cores = cpu_path.use_all_cores()
     fn, units, sample = wl.cpu_sample()

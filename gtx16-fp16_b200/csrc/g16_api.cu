@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include "g16_internal.cuh"
+#include "g16_ptx.cuh"
 
 namespace g16 {
 
@@ -24,11 +25,11 @@ int* g_status_ptr[kMaxDevices] = {};
 std::atomic<uint64_t> g_launches{0};
 thread_local int t_last_cuda = 0;
 
-__global__ void fill_rows_kernel(void* out, int out_f16, const float* bias, int M, int N) {
+__global__ void fill_rows_kernel(void* out, int out_f16, const float* bias, int M, int N, int act) {
   const size_t total = static_cast<size_t>(M) * N;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const float v = bias != nullptr ? bias[i % N] : 0.f;
+    const float v = apply_act(bias != nullptr ? bias[i % N] : 0.f, act);
     if (out_f16)
       reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
     else
@@ -185,8 +186,10 @@ int g16_gemm_auto_ksplit(int M, int K, int N) {
   return gemm_auto_ksplit(M, K, N, *dev);
 }
 
-int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, void* out, int out_dtype, int M, int K,
-             int N, void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+
+int mm_t_impl(const void* x, int x_dtype, const void* w_t, const float* bias, void* out, int out_dtype, int M, int K,
+              int N, void* workspace, size_t workspace_bytes, void* stream, int act) {
   int st = check_common(x, x_dtype, w_t, out, out_dtype, M, K, N);
   if (st != G16_OK) return st;
   if (M == 0 || N == 0) return G16_OK;
@@ -195,14 +198,14 @@ int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, voi
   if (dev == nullptr) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (K == 0) {  // empty reduction: every row is the bias (or zero), like the reference's kernels
-    fill_rows_kernel<<<dev->sm_count * 4, 256, 0, s>>>(out, out_dtype == G16_F16, bias, M, N);
+    fill_rows_kernel<<<dev->sm_count * 4, 256, 0, s>>>(out, out_dtype == G16_F16, bias, M, N, act);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     note_launch();
     return G16_OK;
   }
   if (M <= G16_SKINNY_MAX_M)
-    return launch_skinny(x, x_dtype, static_cast<const uint16_t*>(w_t), bias, out, out_dtype, M, K, N, s, *dev);
+    return launch_skinny(x, x_dtype, static_cast<const uint16_t*>(w_t), bias, out, out_dtype, M, K, N, s, *dev, act);
 
   const MmLayout L = mm_layout(M, K, N, x_dtype, *dev);
   if (L.total > 0) {
@@ -224,7 +227,20 @@ int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, voi
   // the way the reference's fp16 partial sums could.
   // ksplit 0: the automatic plan (L.ksplit sized the workspace for its fallback).
   return launch_gemm(a16, static_cast<const uint16_t*>(w_t), out, out_dtype, bias, rscale, M, K, N, 0,
-                     L.ksplit > 1 ? ws : nullptr, L.partials_bytes, s, *dev);
+                     L.ksplit > 1 ? ws : nullptr, L.partials_bytes, s, *dev, act);
+}
+
+}  // namespace
+
+int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, void* out, int out_dtype, int M, int K,
+             int N, void* workspace, size_t workspace_bytes, void* stream) {
+  return mm_t_impl(x, x_dtype, w_t, bias, out, out_dtype, M, K, N, workspace, workspace_bytes, stream, G16_ACT_NONE);
+}
+
+int g16_mm_t_act(const void* x, int x_dtype, const void* w_t, const float* bias, void* out, int out_dtype, int M,
+                 int K, int N, int act, void* workspace, size_t workspace_bytes, void* stream) {
+  if (act != G16_ACT_NONE && act != G16_ACT_GELU) return G16_ERR_ARG;
+  return mm_t_impl(x, x_dtype, w_t, bias, out, out_dtype, M, K, N, workspace, workspace_bytes, stream, act);
 }
 
 int g16_skinny(const void* x, int x_dtype, const uint16_t* w_t, const float* bias, void* out, int out_dtype, int M,

@@ -70,6 +70,7 @@ struct GemmArgs {
   // Tail split (ksplit == 1): units >= full_units are 128-column halves of the last tiles, so a
   // last partial wave of T tiles runs as 2T half-tiles on the idle SMs (full K, no reduction).
   int full_units, split_tail;
+  int act;  // epilogue activation (G16_ACT_*)
 };
 
 // Scatter epilogue modes.
@@ -140,6 +141,8 @@ __device__ __forceinline__ void store_row32(const GemmArgs& a, int row, int col0
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = v[8 * g + j] * rs;
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = apply_act(o[j], a.act);
     const size_t off = static_cast<size_t>(row) * a.N + col;
     if constexpr (OUT_F16) {
       __half2 h[4];
@@ -485,7 +488,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs args)
     const float rs = args.rscale != nullptr ? __ldg(args.rscale + row) : 1.f;
     float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
     if (args.bias != nullptr) b = __ldg(reinterpret_cast<const float4*>(args.bias + col));
-    const float o0 = fmaf(acc.x, rs, b.x), o1 = fmaf(acc.y, rs, b.y), o2 = fmaf(acc.z, rs, b.z), o3 = fmaf(acc.w, rs, b.w);
+    const float o0 = apply_act(fmaf(acc.x, rs, b.x), args.act), o1 = apply_act(fmaf(acc.y, rs, b.y), args.act),
+                o2 = apply_act(fmaf(acc.z, rs, b.z), args.act), o3 = apply_act(fmaf(acc.w, rs, b.w), args.act);
     const size_t off = static_cast<size_t>(row) * args.N + col;
     if constexpr (OUT_F16) {
       const __half2 h0 = __floats2half2_rn(o0, o1), h1 = __floats2half2_rn(o2, o3);
@@ -579,25 +583,25 @@ cudaError_t launch_reduce(const GemmArgs& args, cudaStream_t s, const DeviceInfo
 
 int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                 const float* rscale, int M, int K, int N, int ksplit, void* ws, size_t ws_bytes, cudaStream_t s,
-                const DeviceInfo& dev) {
+                const DeviceInfo& dev, int act) {
   if (M <= 0 || N <= 0) return G16_OK;
   const int kblocks = (K + kBK - 1) / kBK;
   // Automatic plan, M <= 64: the swapped-operand kernel (weight columns as the MMA's M).
   if (ksplit == 0 && M <= kMidMaxM && G16_MIDM_DISPATCH) {
-    const int st = launch_gemm_midm(a16, b16, out, out_dtype, bias, rscale, M, K, N, s, dev);
+    const int st = launch_gemm_midm(a16, b16, out, out_dtype, bias, rscale, M, K, N, s, dev, act);
     if (st != G16_ERR_UNSUPPORTED) return st;
   }
   if (ksplit == 0) {
     const SmallPlan p = plan_gemm_small(M, K, N, dev);
     if (p.bn != 0) {
-      const int st = launch_gemm_small(a16, b16, out, out_dtype, bias, rscale, M, K, N, p.bn, p.csize, false, s);
+      const int st = launch_gemm_small(a16, b16, out, out_dtype, bias, rscale, M, K, N, p.bn, p.csize, false, s, act);
       if (st != G16_ERR_UNSUPPORTED) return st;
     }
     ksplit = gemm_auto_ksplit(M, K, N, dev);
   }
   if (ksplit > kblocks) ksplit = kblocks;
   if (ksplit > 1 && ksplit <= 16) {
-    const int st = launch_gemm_small(a16, b16, out, out_dtype, bias, rscale, M, K, N, 256, ksplit, true, s);
+    const int st = launch_gemm_small(a16, b16, out, out_dtype, bias, rscale, M, K, N, 256, ksplit, true, s, act);
     if (st != G16_ERR_UNSUPPORTED) return st;
   }
   if (ksplit < 1) ksplit = 1;
@@ -606,11 +610,12 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
   // 4096^3 (+9 %), 8192^3 (+4 %) and 16384 x 16384 x 2048 (+17 %) but lose at N = 16384 (-3 to
   // -20 % depending on the rasterisation), where the single-CTA kernel stays.
   if (ksplit == 1 && N <= 8192 && gemm_pair_available())
-    return launch_gemm_pair(a16, b16, out, out_dtype, bias, rscale, M, K, N, s, dev);
+    return launch_gemm_pair(a16, b16, out, out_dtype, bias, rscale, M, K, N, s, dev, act);
   GemmArgs args{};
   args.out = out;
   args.bias = bias;
   args.rscale = rscale;
+  args.act = act;
   args.status = device_status_ptr();
   if (args.status == nullptr) return G16_ERR_CUDA;
   args.M = M;

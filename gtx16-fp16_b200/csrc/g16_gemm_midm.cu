@@ -66,6 +66,7 @@ struct MidArgs {
   int M, N, K;
   int kchunk;  // K rows per cluster rank (a multiple of 64)
   int stages;  // ring depth
+  int act;     // epilogue activation (G16_ACT_*)
 };
 
 template <int MX, bool OUT_F16>
@@ -283,7 +284,7 @@ gemm_midm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             const int m = c * 32 + e;
             if (m < args.M) {
               const float rs = args.rscale != nullptr ? __ldg(args.rscale + m) : 1.f;
-              const float o = fmaf(v[e], rs, b);
+              const float o = apply_act(fmaf(v[e], rs, b), args.act);
               if constexpr (OUT_F16) {
                 reinterpret_cast<__half*>(args.out)[static_cast<size_t>(m) * args.N + n] = __float2half_rn(o);
               } else {
@@ -333,7 +334,7 @@ gemm_midm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             const int m = 4 * m4 + e;
             if (m < args.M) {
               const float rs = args.rscale != nullptr ? __ldg(args.rscale + m) : 1.f;
-              const float o = fmaf(a4[e], rs, b);
+              const float o = apply_act(fmaf(a4[e], rs, b), args.act);
               if constexpr (OUT_F16) {
                 reinterpret_cast<__half*>(args.out)[static_cast<size_t>(m) * args.N + nn] = __float2half_rn(o);
               } else {
@@ -449,7 +450,7 @@ int md_plan_for(F* kern, int M, int K, int N, const DeviceInfo& dev, MidPlan* ou
 
 template <int MX, bool OUT_F16>
 int md_launch_t(const uint16_t* x16, const uint16_t* w, void* out, const float* bias, const float* rscale, int M,
-                int K, int N, cudaStream_t s, const DeviceInfo& dev) {
+                int K, int N, cudaStream_t s, const DeviceInfo& dev, int act) {
   static std::atomic<uint64_t> attr_done{0};
   auto kern = gemm_midm_kernel<MX, OUT_F16>;
   cudaError_t e = md_ensure_attrs(kern, attr_done, 227 * 1024);
@@ -476,6 +477,7 @@ int md_launch_t(const uint16_t* x16, const uint16_t* w, void* out, const float* 
   a.K = K;
   a.kchunk = p.kchunk;
   a.stages = p.stages;
+  a.act = act;
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = md_cfg(p, s, attr);
   e = cudaLaunchKernelEx(&cfg, kern, tx, tw, a);
@@ -486,9 +488,9 @@ int md_launch_t(const uint16_t* x16, const uint16_t* w, void* out, const float* 
 
 template <int MX>
 int md_launch_m(const uint16_t* x16, const uint16_t* w, void* out, int out_dtype, const float* bias,
-                const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev) {
-  return out_dtype == G16_F16 ? md_launch_t<MX, true>(x16, w, out, bias, rscale, M, K, N, s, dev)
-                              : md_launch_t<MX, false>(x16, w, out, bias, rscale, M, K, N, s, dev);
+                const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act) {
+  return out_dtype == G16_F16 ? md_launch_t<MX, true>(x16, w, out, bias, rscale, M, K, N, s, dev, act)
+                              : md_launch_t<MX, false>(x16, w, out, bias, rscale, M, K, N, s, dev, act);
 }
 
 }  // namespace
@@ -499,12 +501,12 @@ int gemm_midm_ranks(int M, int K, int N, const DeviceInfo& dev) {
 }
 
 int launch_gemm_midm(const uint16_t* x16, const uint16_t* w, void* out, int out_dtype, const float* bias,
-                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev) {
+                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act) {
   if (M <= 0 || N <= 0) return G16_OK;
   if (M > kMidMaxM || K <= 0) return G16_ERR_UNSUPPORTED;
-  if (M <= 16) return md_launch_m<16>(x16, w, out, out_dtype, bias, rscale, M, K, N, s, dev);
-  if (M <= 32) return md_launch_m<32>(x16, w, out, out_dtype, bias, rscale, M, K, N, s, dev);
-  return md_launch_m<64>(x16, w, out, out_dtype, bias, rscale, M, K, N, s, dev);
+  if (M <= 16) return md_launch_m<16>(x16, w, out, out_dtype, bias, rscale, M, K, N, s, dev, act);
+  if (M <= 32) return md_launch_m<32>(x16, w, out, out_dtype, bias, rscale, M, K, N, s, dev, act);
+  return md_launch_m<64>(x16, w, out, out_dtype, bias, rscale, M, K, N, s, dev, act);
 }
 
 }  // namespace g16

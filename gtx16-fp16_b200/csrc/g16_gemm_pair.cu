@@ -50,6 +50,7 @@ struct PairArgs {
   int* status;
   int M, N, K;
   int m2_tiles, n_tiles, units, kblocks;  // tiles of 256 x 256
+  int act;                                // epilogue activation (G16_ACT_*)
 };
 
 __device__ __forceinline__ void pair_coords(const PairArgs& a, int u, int* mt2, int* nt) {
@@ -80,6 +81,8 @@ __device__ __forceinline__ void pair_pack32(const PairArgs& a, int col0, float r
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = __uint_as_float(r[8 * g + j]) * rs;
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = apply_act(o[j], a.act);
     if constexpr (OUT_F16) {
       __half2 h[4];
 #pragma unroll
@@ -354,9 +357,10 @@ bool gemm_pair_available() {
 }
 
 int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
-                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev) {
+                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act) {
   if (M <= 0 || N <= 0) return G16_OK;
   PairArgs args{};
+  args.act = act;
   args.out = out;
   args.bias = bias;
   args.rscale = rscale;

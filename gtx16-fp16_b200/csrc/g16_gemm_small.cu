@@ -54,11 +54,16 @@ struct SmallArgs {
   int M, N, K;
   int n_tiles;           // tiles along N
   int kblocks, kb_per_split;
+  int act;  // epilogue activation (G16_ACT_*)
 };
 
 template <bool OUT_F16>
 __device__ __forceinline__ void store4(const SmallArgs& a, int row, int col, float o0, float o1, float o2, float o3) {
   const size_t off = static_cast<size_t>(row) * a.N + col;
+  o0 = apply_act(o0, a.act);
+  o1 = apply_act(o1, a.act);
+  o2 = apply_act(o2, a.act);
+  o3 = apply_act(o3, a.act);
   if constexpr (OUT_F16) {
     const __half2 h0 = __floats2half2_rn(o0, o1), h1 = __floats2half2_rn(o2, o3);
     uint2 u;
@@ -298,12 +303,13 @@ cudaError_t ensure_small_attrs(F* kern, std::atomic<uint64_t>& done, int bytes) 
 
 template <bool OUT_F16, int BN>
 int launch_small_t(const uint16_t* a16, const uint16_t* b16, void* out, const float* bias, const float* rscale, int M,
-                   int K, int N, int csize, cudaStream_t s) {
+                   int K, int N, int csize, cudaStream_t s, int act) {
   static std::atomic<uint64_t> attr_done{0};
   auto kern = gemm_small_kernel<OUT_F16, BN>;
   cudaError_t e = ensure_small_attrs(kern, attr_done, static_cast<int>(SmallGeo<BN>::kSmemBytes));
   if (e != cudaSuccess) return cuda_fail(e);
   SmallArgs args{};
+  args.act = act;
   args.out = out;
   args.bias = bias;
   args.rscale = rscale;
@@ -429,18 +435,19 @@ SmallPlan plan_gemm_small(int M, int K, int N, const DeviceInfo& dev) {
 }
 
 int launch_gemm_small(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
-                      const float* rscale, int M, int K, int N, int bn, int csize, bool exact, cudaStream_t s) {
+                      const float* rscale, int M, int K, int N, int bn, int csize, bool exact, cudaStream_t s,
+                      int act) {
   if (csize < 1 || csize > kSmMaxCluster || (bn != 128 && bn != 256)) return G16_ERR_ARG;
   const int tiles = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
   int c = csize;
   while (c > 1 && active_clusters_bn(bn, c, tiles) < 1) --c;  // a cluster must fit at all
   if (exact && c != csize) return G16_ERR_UNSUPPORTED;        // the caller asked for csize K chunks
   if (out_dtype == G16_F16) {
-    return bn == 128 ? launch_small_t<true, 128>(a16, b16, out, bias, rscale, M, K, N, c, s)
-                     : launch_small_t<true, 256>(a16, b16, out, bias, rscale, M, K, N, c, s);
+    return bn == 128 ? launch_small_t<true, 128>(a16, b16, out, bias, rscale, M, K, N, c, s, act)
+                     : launch_small_t<true, 256>(a16, b16, out, bias, rscale, M, K, N, c, s, act);
   }
-  return bn == 128 ? launch_small_t<false, 128>(a16, b16, out, bias, rscale, M, K, N, c, s)
-                   : launch_small_t<false, 256>(a16, b16, out, bias, rscale, M, K, N, c, s);
+  return bn == 128 ? launch_small_t<false, 128>(a16, b16, out, bias, rscale, M, K, N, c, s, act)
+                   : launch_small_t<false, 256>(a16, b16, out, bias, rscale, M, K, N, c, s, act);
 }
 
 }  // namespace g16

@@ -30,7 +30,7 @@ void note_launch(uint64_t n = 1);
 
 // ---- launchers (host), each returns a g16_status code ----
 int launch_skinny(const void* x, int x_dtype, const uint16_t* w, const float* bias, void* out, int out_dtype, int M,
-                  int K, int N, cudaStream_t s, const DeviceInfo& dev);
+                  int K, int N, cudaStream_t s, const DeviceInfo& dev, int act = 0);
 
 // Launch plan of the skinny kernel for (M, K, N): info[0] tensor-core variant (1) or FMA (0),
 // [1] cluster size, [2] strips, [3] K chunk, [4] dynamic shared memory, [5] resident clusters at the
@@ -47,7 +47,7 @@ int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, in
 // or ksplit > 16; ws must then hold gemm_workspace_bytes(M, K, N, ksplit)).
 int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                 const float* rscale, int M, int K, int N, int ksplit, void* ws, size_t ws_bytes, cudaStream_t s,
-                const DeviceInfo& dev);
+                const DeviceInfo& dev, int act = 0);
 size_t gemm_workspace_bytes(int M, int K, int N, int ksplit);
 // Sharded GEMM whose fp16/fp32 output tiles go to ndst buffers [M, ldc] at column col0 (no split-K).
 int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
@@ -57,14 +57,14 @@ int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
 
 // GEMM on CTA pairs (g16_gemm_pair.cu): persistent, 256 x 256 tiles, tcgen05.mma.cta_group::2.
 int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
-                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev);
+                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act = 0);
 bool gemm_pair_available();
 
 // Medium-M GEMM (g16_gemm_midm.cu): M <= kMidMaxM activation rows, operands swapped so the
 // weight columns are the MMA's M and the rows its N; K split over a cluster, reduced in DSMEM.
 constexpr int kMidMaxM = 64;
 int launch_gemm_midm(const uint16_t* x16, const uint16_t* w, void* out, int out_dtype, const float* bias,
-                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev);
+                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act = 0);
 // Cluster size (K ranks) of the medium-M plan for this shape, 0 when it does not apply.
 int gemm_midm_ranks(int M, int K, int N, const DeviceInfo& dev);
 
@@ -77,7 +77,7 @@ struct SmallPlan {
 SmallPlan plan_gemm_small(int M, int K, int N, const DeviceInfo& dev);
 // exact: fail with G16_ERR_UNSUPPORTED rather than run fewer K chunks than csize.
 int launch_gemm_small(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
-                      const float* rscale, int M, int K, int N, int bn, int csize, bool exact, cudaStream_t s);
+                      const float* rscale, int M, int K, int N, int bn, int csize, bool exact, cudaStream_t s, int act = 0);
 
 // 2-D TMA tensor map over a row-major [rows, cols] matrix with a [box_rows, box_cols] box (g16_tmap.cu).
 int make_tmap_2d_strided(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes,

@@ -310,6 +310,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Epilogue activation (G16_ACT_*), applied to the fp32 value after the bias. GELU is the exact
+// erf form, evaluated as x * 0.5 * (1 + erf(x / sqrt(2))) in fp32 (the order torch's GELU uses).
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == 1) return v * 0.5f * (1.f + erff(v * 0.70710678118654752440f));
+  return v;
+}
+
 // Shared-memory matrix descriptor (sm_100 format): start address, leading / stride byte offsets
 // (all >> 4), version 1 at bit 46, swizzle mode in bits 61-63 (2 = 128-byte swizzle).
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {

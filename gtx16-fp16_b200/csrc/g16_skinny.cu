@@ -87,6 +87,7 @@ struct SkinnyArgs {
   int K, N, kchunk, piece;
   int stages;  // tensor-core variant: weight ring depth
   int rows;    // tensor-core variant: weight rows per stage (32, 64 or 128)
+  int act;     // epilogue activation (G16_ACT_*)
 };
 
 // grid = (C, strips); cluster = (C, 1, 1); blockIdx.x is the CTA's rank in its cluster and selects
@@ -268,6 +269,7 @@ skinny_fma_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs a
         for (int q = 0; q < kMaxCluster; ++q)
           if (q < csize) s += pv[q];
         if (args.bias != nullptr) s += args.bias[n];
+        s = apply_act(s, args.act);
         if constexpr (OUT_F16) {
           reinterpret_cast<__half*>(args.out)[static_cast<size_t>(m) * args.N + n] = __float2half_rn(s);
         } else {
@@ -392,7 +394,7 @@ int plan_for(F* kern, int M, int K, int N, const DeviceInfo& dev, SkinnyPlan* ou
 
 template <int M, typename TX, bool OUT_F16>
 int launch_skinny_fma_t(const void* x, const uint16_t* w, const float* bias, void* out, int K, int N, cudaStream_t s,
-                        const DeviceInfo& dev) {
+                        const DeviceInfo& dev, int act) {
   static std::atomic<uint64_t> attr_done{0};
   auto kern = skinny_fma_kernel<M, TX, OUT_F16>;
   cudaError_t e = ensure_attrs(kern, attr_done, kSmemAttrBytes);
@@ -407,6 +409,7 @@ int launch_skinny_fma_t(const void* x, const uint16_t* w, const float* bias, voi
                         kBoxRows, kStrip, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st != G16_OK) return st;
   SkinnyArgs a{};
+  a.act = act;
   a.x = x;
   a.bias = bias;
   a.out = out;
@@ -846,6 +849,7 @@ skinny_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const SkinnyArgs ar
         float acc = 0.f;
         for (int q = 0; q < csize; ++q) acc += red[(q * slice + jj) * MP + m];
         if (args.bias != nullptr) acc += args.bias[n];
+        acc = apply_act(acc, args.act);
         if constexpr (OUT_F16) {
           reinterpret_cast<__half*>(args.out)[static_cast<size_t>(m) * args.N + n] = __float2half_rn(acc);
         } else {
@@ -968,7 +972,7 @@ int plan_tc_for(F* kern, int M, int K, int N, int x_bytes, const DeviceInfo& dev
 
 template <int M, typename TX, bool OUT_F16>
 int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void* out, int K, int N, cudaStream_t s,
-                       const DeviceInfo& dev) {
+                       const DeviceInfo& dev, int act) {
   static std::atomic<uint64_t> attr_done{0};
   auto kern = skinny_tc_kernel<M, TX, OUT_F16>;
   cudaError_t e = ensure_attrs(kern, attr_done, kTcSmemLimit);
@@ -976,7 +980,7 @@ int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void
   SkinnyPlan p;
   int st = plan_tc_for(kern, M, K, N, static_cast<int>(sizeof(TX)), dev, &p);
   if (st != G16_OK) return st;
-  if (!p.tc) return launch_skinny_fma_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev);
+  if (!p.tc) return launch_skinny_fma_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev, act);
   if (p.stages < 2 || p.stages > kTcMaxStages ||
       p.smem_bytes != skinny_tc_smem_bytes(M, p.kchunk, p.rows, p.stages) ||
       p.stages < tc_xst_stages(M, p.kchunk, static_cast<int>(sizeof(TX)), p.rows) + 1 ||
@@ -987,6 +991,7 @@ int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void
                     p.rows, kTcBoxCols, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
   SkinnyArgs a{};
+  a.act = act;
   a.x = x;
   a.bias = bias;
   a.out = out;
@@ -1015,34 +1020,34 @@ int launch_skinny_tc_t(const void* x, const uint16_t* w, const float* bias, void
 // The tensor-core variant whenever its K chunk fits in shared memory, else the FMA variant.
 template <int M, typename TX, bool OUT_F16>
 int launch_skinny_t(const void* x, const uint16_t* w, const float* bias, void* out, int K, int N, cudaStream_t s,
-                    const DeviceInfo& dev) {
-  return launch_skinny_tc_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev);
+                    const DeviceInfo& dev, int act) {
+  return launch_skinny_tc_t<M, TX, OUT_F16>(x, w, bias, out, K, N, s, dev, act);
 }
 
 template <int M>
 int dispatch_types(const void* x, int x_dtype, const uint16_t* w, const float* bias, void* out, int out_dtype, int K,
-                   int N, cudaStream_t s, const DeviceInfo& dev) {
+                   int N, cudaStream_t s, const DeviceInfo& dev, int act) {
   if (x_dtype == G16_F32) {
-    return out_dtype == G16_F16 ? launch_skinny_t<M, float, true>(x, w, bias, out, K, N, s, dev)
-                                : launch_skinny_t<M, float, false>(x, w, bias, out, K, N, s, dev);
+    return out_dtype == G16_F16 ? launch_skinny_t<M, float, true>(x, w, bias, out, K, N, s, dev, act)
+                                : launch_skinny_t<M, float, false>(x, w, bias, out, K, N, s, dev, act);
   }
-  return out_dtype == G16_F16 ? launch_skinny_t<M, __half, true>(x, w, bias, out, K, N, s, dev)
-                              : launch_skinny_t<M, __half, false>(x, w, bias, out, K, N, s, dev);
+  return out_dtype == G16_F16 ? launch_skinny_t<M, __half, true>(x, w, bias, out, K, N, s, dev, act)
+                              : launch_skinny_t<M, __half, false>(x, w, bias, out, K, N, s, dev, act);
 }
 
 }  // namespace
 
 int launch_skinny(const void* x, int x_dtype, const uint16_t* w, const float* bias, void* out, int out_dtype, int M,
-                  int K, int N, cudaStream_t s, const DeviceInfo& dev) {
+                  int K, int N, cudaStream_t s, const DeviceInfo& dev, int act) {
   switch (M) {
-    case 1: return dispatch_types<1>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
-    case 2: return dispatch_types<2>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
-    case 3: return dispatch_types<3>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
-    case 4: return dispatch_types<4>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
-    case 5: return dispatch_types<5>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
-    case 6: return dispatch_types<6>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
-    case 7: return dispatch_types<7>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
-    case 8: return dispatch_types<8>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev);
+    case 1: return dispatch_types<1>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev, act);
+    case 2: return dispatch_types<2>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev, act);
+    case 3: return dispatch_types<3>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev, act);
+    case 4: return dispatch_types<4>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev, act);
+    case 5: return dispatch_types<5>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev, act);
+    case 6: return dispatch_types<6>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev, act);
+    case 7: return dispatch_types<7>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev, act);
+    case 8: return dispatch_types<8>(x, x_dtype, w, bias, out, out_dtype, K, N, s, dev, act);
     default: return G16_ERR_ARG;
   }
 }

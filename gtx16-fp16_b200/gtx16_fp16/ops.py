@@ -82,13 +82,20 @@ def _ws_bytes(dev_index: int, M: int, K: int, N: int, xcode: int) -> int:
     return n
 
 
+_ACTS = {None: _native.ACT_NONE, "gelu": _native.ACT_GELU}
+
+
 def mm_t(x2d: torch.Tensor, w_t: torch.Tensor, bias: torch.Tensor | None = None,
-         out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+         out_dtype: torch.dtype = torch.float32, *, act: str | None = None) -> torch.Tensor:
     """out[M,N] = x2d[M,K] @ w_t[K,N] + bias[N].
 
     x2d fp16 or fp32 (fp32 rows with |max| > 1024 are rescaled by a power of two before the fp16
     cast on the GEMM path); w_t fp16; bias fp32 or None; out fp32 or fp16, always a fresh tensor.
-    Check supported() first: unlike the reference, an unsupported input raises ValueError."""
+    Check supported() first: unlike the reference, an unsupported input raises ValueError.
+    act="gelu" (keyword, not in the reference) applies the exact GELU in the epilogue:
+    gelu(x2d @ w_t + bias), computed in fp32 before the output cast."""
+    if act not in _ACTS:
+        raise ValueError(f"act must be None or 'gelu', got {act!r}")
     if out_dtype not in (torch.float32, torch.float16):
         raise ValueError(f"out_dtype must be float32 or float16, got {out_dtype}")
     if not supported(x2d, w_t):
@@ -110,16 +117,21 @@ def mm_t(x2d: torch.Tensor, w_t: torch.Tensor, bias: torch.Tensor | None = None,
     xcode = dtype_code(x.dtype)
     if idx != torch.cuda.current_device():
         with torch.cuda.device(idx):
-            return _mm_t_launch(lib, x, w_t, b, out, xcode, M, K, N, dev, idx)
-    return _mm_t_launch(lib, x, w_t, b, out, xcode, M, K, N, dev, idx)
+            return _mm_t_launch(lib, x, w_t, b, out, xcode, M, K, N, dev, idx, _ACTS[act])
+    return _mm_t_launch(lib, x, w_t, b, out, xcode, M, K, N, dev, idx, _ACTS[act])
 
 
-def _mm_t_launch(lib, x, w_t, b, out, xcode, M, K, N, dev, idx):
+def _mm_t_launch(lib, x, w_t, b, out, xcode, M, K, N, dev, idx, act=_native.ACT_NONE):
     stream = stream_handle(idx)
     need = _ws_bytes(idx, M, K, N, xcode)
     ws, wsn = _native.workspace(dev, stream, need)
-    st = lib.g16_mm_t(x.data_ptr(), xcode, w_t.data_ptr(), None if b is None else b.data_ptr(), out.data_ptr(),
-                      dtype_code(out.dtype), M, K, N, ws or None, wsn, stream)
+    bp = None if b is None else b.data_ptr()
+    if act == _native.ACT_NONE:
+        st = lib.g16_mm_t(x.data_ptr(), xcode, w_t.data_ptr(), bp, out.data_ptr(), dtype_code(out.dtype), M, K, N,
+                          ws or None, wsn, stream)
+    else:
+        st = lib.g16_mm_t_act(x.data_ptr(), xcode, w_t.data_ptr(), bp, out.data_ptr(), dtype_code(out.dtype), M, K, N,
+                              act, ws or None, wsn, stream)
     if st != _native.OK:
         raise G16Error(st, "g16_mm_t")
     return out

@@ -64,6 +64,14 @@ enum g16_status {
 int g16_mm_t(const void* x, int x_dtype, const void* w_t, const float* bias, void* out, int out_dtype, int M, int K,
              int N, void* workspace, size_t workspace_bytes, void* stream);
 
+/* g16_mm_t with an activation applied by the epilogue after the bias: out = act(x @ w_t + bias)
+ * (no counterpart in the reference; `patch(..., fuse=True)` folds a Linear's GELU into its GEMM
+ * with it). act: G16_ACT_NONE or G16_ACT_GELU (exact erf form, x * 0.5 * (1 + erf(x / sqrt(2)))
+ * in fp32 before the output cast). Same workspace as g16_mm_t; G16_ERR_ARG for another act. */
+enum g16_act { G16_ACT_NONE = 0, G16_ACT_GELU = 1 };
+int g16_mm_t_act(const void* x, int x_dtype, const void* w_t, const float* bias, void* out, int out_dtype, int M,
+                 int K, int N, int act, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of workspace g16_mm_t needs for this problem on the current device (0 when none). */
 size_t g16_mm_t_workspace_bytes(int M, int K, int N, int x_dtype);
 

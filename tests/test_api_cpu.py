@@ -131,3 +131,59 @@ def test_fast_linear_keeps_its_storage_formats_under_dtype_casts():
 def test_patch_rejects_unknown_activation_dtype():
     with pytest.raises(ValueError, match="activations"):
         g.patch(nn.Sequential(nn.Linear(8, 8)), force=True, activations=torch.bfloat16)
+
+
+class _Intermediate(nn.Module):  # the shape of transformers' BertIntermediate
+    def __init__(self):
+        super().__init__()
+        import transformers.activations as ta
+        self.dense = g.FastLinear(64, 128)
+        self.intermediate_act_fn = ta.ACT2FN["gelu"]
+
+    def forward(self, x):
+        return self.intermediate_act_fn(self.dense(x))
+
+
+class _Attention(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.query, self.key, self.value = g.FastLinear(64, 64), g.FastLinear(64, 64), g.FastLinear(64, 32)
+
+    def forward(self, x):
+        return self.query(x), self.key(x), self.value(x)
+
+
+def _init(m):
+    torch.manual_seed(0)
+    for mod in m.modules():
+        if isinstance(mod, g.FastLinear):
+            with torch.no_grad():
+                mod.weight_t.copy_((torch.randn(mod.in_features, mod.out_features) * 0.1).half())
+                mod.bias.copy_(torch.randn(mod.out_features))
+    return m
+
+
+def test_fuse_rewrites_gelu_and_groups_qkv_on_cpu():
+    """patch(fuse=True)'s rewrite: the exact GELU after `dense` (and after a FastLinear inside an
+    nn.Sequential) moves into the layer (activation='gelu', the GELU module becomes Identity); the
+    query/key/value layers form one shared-input group; a tanh-approximate GELU is left alone.
+    The CPU fallback computes the same function before and after."""
+    from gtx16_fp16.linear import _fuse
+    inter = _init(_Intermediate())
+    seq = _init(nn.Sequential(g.FastLinear(64, 64), nn.GELU(), g.FastLinear(64, 64), nn.GELU(approximate="tanh")))
+    att = _init(_Attention())
+    model = nn.ModuleDict({"inter": inter, "seq": seq, "att": att})
+    x = torch.randn(5, 64)
+    with torch.no_grad():
+        before = [inter(x), seq(x), *att(x)]
+    assert _fuse(model) == (2, 1)
+    assert inter.dense.activation == "gelu" and isinstance(inter.intermediate_act_fn, nn.Identity)
+    assert seq[0].activation == "gelu" and isinstance(seq[1], nn.Identity)
+    assert seq[2].activation is None and isinstance(seq[3], nn.GELU)
+    assert att.query._group is att.key._group is att.value._group is not None
+    assert "fused_group=2/3" in repr(att.value)
+    with torch.no_grad():
+        after = [inter(x), seq(x), *att(x)]
+    for a, b in zip(before, after):
+        torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-6)
+    assert _fuse(model) == (0, 0)  # idempotent

@@ -62,6 +62,40 @@ def test_bert_base_fp16_activations_mode(cuda_ok):
     assert cos.min().item() >= 0.9999, cos.min().item()  # measured 0.9999987 on B200
 
 
+@pytest.mark.parametrize("half", [False, True])
+def test_bert_base_fused_patch(cuda_ok, half):
+    """patch(..., fuse=True): the 12 intermediate GELUs fold into their GEMMs and each attention's
+    query/key/value share one GEMM. Same CLS embeddings as the unfused patch (up to rounding) and
+    the fp32 model's within cosine 0.9999; in fp32 mode 12 x 2 fewer rowscale passes and 12 fewer
+    GELU launches."""
+    transformers = pytest.importorskip("transformers")
+    cfg = transformers.BertConfig(vocab_size=30522, hidden_size=768, num_hidden_layers=12, num_attention_heads=12,
+                                  intermediate_size=3072, hidden_act="gelu", max_position_embeddings=512,
+                                  attn_implementation="sdpa")
+    torch.manual_seed(0)
+    model = transformers.BertModel(cfg).eval()
+    ref_model = copy.deepcopy(model).cuda()
+    plain = copy.deepcopy(model).cuda()
+    model = model.cuda()
+    act = torch.float16 if half else None
+    assert g.patch(plain, force=True, activations=act) == 73
+    assert g.patch(model, force=True, activations=act, fuse=True) == 73
+    layer = model.encoder.layer[0]
+    assert layer.intermediate.dense.activation == "gelu"
+    assert isinstance(layer.intermediate.intermediate_act_fn, torch.nn.Identity)
+    assert layer.attention.self.query._group is layer.attention.self.value._group is not None
+    gen = torch.Generator().manual_seed(0)
+    ids = torch.randint(1000, 30522, (8, 256), generator=gen).cuda()
+    mask = torch.ones_like(ids)
+    with torch.no_grad():
+        ref = ref_model(input_ids=ids, attention_mask=mask).last_hidden_state[:, 0].float()
+        unf = plain(input_ids=ids, attention_mask=mask).last_hidden_state[:, 0].float()
+        got = model(input_ids=ids, attention_mask=mask).last_hidden_state[:, 0].float()
+    torch.testing.assert_close(got, unf, rtol=1e-2 if half else 1e-4, atol=1e-2 if half else 1e-4)
+    cos = (torch.nn.functional.normalize(ref, dim=-1) * torch.nn.functional.normalize(got, dim=-1)).sum(-1)
+    assert cos.min().item() >= 0.9999, cos.min().item()
+
+
 @pytest.mark.parametrize("M,K,N", [(512, 1024, 2048), (300, 512, 776)])
 def test_sharded_matmul_single_gpu(cuda_ok, M, K, N):
     torch.manual_seed(0)

@@ -6,6 +6,7 @@ import ctypes
 import pytest
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 import gtx16_fp16 as g
 from gtx16_fp16 import _native
@@ -369,6 +370,42 @@ def test_rowscale_row_lengths(cuda_ok, xdt, K):
     assert torch.equal(S.cpu(), exp_s)
     assert S[1].item() == 2.0 and S[2].item() == 1.0
     assert torch.equal(y, (x.float() / S[:, None]).half())
+
+
+# shapes reaching each epilogue: skinny (M <= 8, fp32 x), medium-M, small-problem (cluster split),
+# CTA pairs, single-CTA persistent (N > 8192), and the empty reduction
+GELU_SHAPES = [(1, 1024, 3072), (4, 4096, 512), (16, 1024, 3072), (64, 768, 3072), (256, 768, 3072),
+               (128, 16384, 1024), (4096, 768, 3072), (512, 256, 12288), (40, 0, 136)]
+
+
+@pytest.mark.parametrize("M,K,N", GELU_SHAPES)
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+def test_mm_t_gelu_epilogue(cuda_ok, M, K, N, out_dtype):
+    """mm_t(..., act="gelu") applies the exact GELU to the fp32 epilogue value: it equals torch's
+    F.gelu of the plain result (fp32 output) to an ulp, and the fp16 output is that value rounded."""
+    torch.manual_seed(M + K + N)
+    x = torch.randn(M, K, device="cuda")
+    w = (torch.randn(K, N, device="cuda") * (max(K, 1) ** -0.5)).half()
+    b = torch.randn(N, device="cuda")
+    plain = g.mm_t(x, w, b, torch.float32)
+    ref = F.gelu(plain)
+    y = g.mm_t(x, w, b, out_dtype, act="gelu")
+    if out_dtype == torch.float32:
+        torch.testing.assert_close(y, ref, rtol=2e-6, atol=2e-7)
+    else:
+        torch.testing.assert_close(y.float(), ref.half().float(), rtol=1e-3, atol=1e-3)
+    with pytest.raises(ValueError):
+        g.mm_t(x, w, b, out_dtype, act="relu")
+
+
+def test_mm_t_act_rejects_unknown_code(cuda_ok):
+    L = _native.lib()
+    x = torch.randn(16, 64, device="cuda")
+    w = torch.randn(64, 64, device="cuda").half()
+    out = torch.empty(16, 64, device="cuda")
+    st = L.g16_mm_t_act(x.data_ptr(), _native.G16_F32, w.data_ptr(), None, out.data_ptr(), _native.G16_F32, 16, 64,
+                        64, 7, None, 0, _native.stream_handle(0))
+    assert st == _native.ERR_ARG
 
 
 def test_k_zero_gives_bias(cuda_ok):
