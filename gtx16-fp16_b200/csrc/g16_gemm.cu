@@ -606,10 +606,10 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
   }
   if (ksplit < 1) ksplit = 1;
   // A single pass runs on CTA pairs (256 x 256 tiles, a third fewer operand bytes per FLOP; the
-  // same bits as the single-CTA kernel below) up to N = 8192: measured on B200, pairs win at
-  // 4096^3 (+9 %), 8192^3 (+4 %) and 16384 x 16384 x 2048 (+17 %) but lose at N = 16384 (-3 to
-  // -20 % depending on the rasterisation), where the single-CTA kernel stays.
-  if (ksplit == 1 && N <= 8192 && gemm_pair_available())
+  // same bits as the single-CTA kernel below). Measured on B200 with the pair kernel's TMA-store
+  // epilogue: 4096^3 +9 %, 16384^3 +4-10 %, 8192 x 8192 x 16384 +7-14 %, 4096 x 4096 x 16384
+  // +17-23 % over the single-CTA kernel, which keeps the multi-destination scatter epilogue.
+  if (ksplit == 1 && gemm_pair_available())
     return launch_gemm_pair(a16, b16, out, out_dtype, bias, rscale, M, K, N, s, dev, act);
   GemmArgs args{};
   args.out = out;

@@ -37,7 +37,10 @@ constexpr uint32_t kPrBBoxBytes = kBK * 64 * 2;     // [64 k x 64 n]: 8 KiB
 constexpr uint32_t kPrBBytes = 2 * kPrBBoxBytes;    // this CTA's 128-column half of B
 constexpr uint32_t kPrStageBytes = kPrABytes + kPrBBytes;  // 32 KiB per CTA
 constexpr uint32_t kPrTmemCols = 2 * kBN;           // two 256-column accumulators
-constexpr int kPrGroupM = 8;                        // rasterisation: 8 pair-rows (2048 rows) per group
+// Rasterisation: 8 pair-rows (2048 rows) per group. Measured against 4 and 16 at 16384^3,
+// 8192 x 8192 x 16384, 4096 x 4096 x 16384 and 16384 x 16384 x 8192: best or within the
+// run-to-run spread on each.
+constexpr int kPrGroupM = 8;
 constexpr uint32_t kPrEpiBufBytes = 32 * 128;             // one warp's 32 rows x 128 bytes
 constexpr uint32_t kPrEpiBytes = kPrEpiWarps * 2 * kPrEpiBufBytes;  // two buffers per epilogue warp
 constexpr size_t kPrSmemBytes = 1024 + kPrStages * kPrStageBytes + kPrEpiBytes + 256;

@@ -247,12 +247,11 @@ def test_automatic_small_problem_plan(cuda_ok, M, K, N, out_dtype):
                                    (1000, 776, 12296)])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 def test_persistent_gemm_single_pass(cuda_ok, M, K, N, out_dtype):
-    """Explicit single-pass GEMMs (ksplit = 1): N <= 8192 on CTA pairs (256 x 256 tiles), every tile
-    over the whole K; wider outputs on the single-CTA kernel, whose last partial wave runs as
-    128-column halves when it fits in half the SMs (512 x 12288: 192 tiles on 148 SMs, the last 44
-    as 88 halves). Deterministic, bitwise equal to the single-CTA kernel (reached through the
-    one-destination scatter entry point), within the GEMM tolerance, bias on every column including
-    ragged last tiles."""
+    """Explicit single-pass GEMMs (ksplit = 1) run on CTA pairs (256 x 256 tiles, every tile over the
+    whole K), N = 12288 and 12296 included. Deterministic, bitwise equal to the single-CTA kernel
+    (reached through the one-destination scatter entry point, whose last partial wave runs as
+    128-column halves when it fits in half the SMs: 512 x 12288 has 192 tiles on 148 SMs, the last
+    44 as 88 halves), within the GEMM tolerance, bias on every column including ragged last tiles."""
     gen = torch.Generator(device="cuda").manual_seed(M + K + N)
     a = torch.randn(M, K, device="cuda", generator=gen).half()
     b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
@@ -373,7 +372,7 @@ def test_rowscale_row_lengths(cuda_ok, xdt, K):
 
 
 # shapes reaching each epilogue: skinny (M <= 8, fp32 x), medium-M, small-problem (cluster split),
-# CTA pairs, single-CTA persistent (N > 8192), and the empty reduction
+# CTA pairs (N = 12288 included), and the empty reduction
 GELU_SHAPES = [(1, 1024, 3072), (4, 4096, 512), (16, 1024, 3072), (64, 768, 3072), (256, 768, 3072),
                (128, 16384, 1024), (4096, 768, 3072), (512, 256, 12288), (40, 0, 136)]
 
