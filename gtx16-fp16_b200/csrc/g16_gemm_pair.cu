@@ -46,6 +46,15 @@ constexpr uint32_t kPrEpiBytes = kPrEpiWarps * 2 * kPrEpiBufBytes;  // two buffe
 constexpr size_t kPrSmemBytes = 1024 + kPrStages * kPrStageBytes + kPrEpiBytes + 256;
 static_assert(kPrSmemBytes <= 227 * 1024, "pair GEMM shared memory");
 
+// Output tensor maps: one for a plain GEMM, or one per destination of the multi-GPU scatter (each
+// [M, col0 + N] of a [.., ldc] buffer; this GEMM's tile lands at column col0 of every one).
+constexpr int kPrMaxDst = G16_SCATTER_MAX_DST;
+struct PairDst {
+  CUtensorMap m[kPrMaxDst];
+  int ndst;
+  int col0;
+};
+
 struct PairArgs {
   void* out;
   const float* bias;
@@ -103,7 +112,7 @@ __device__ __forceinline__ void pair_pack32(const PairArgs& a, int col0, float r
 template <bool OUT_F16>
 __global__ void __launch_bounds__(kPrThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                 const __grid_constant__ CUtensorMap tmap_out,
+                 const __grid_constant__ PairDst dst,
                  const PairArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -147,7 +156,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
-    tma_prefetch_desc(&tmap_out);
+    for (int d = 0; d < dst.ndst; ++d) tma_prefetch_desc(&dst.m[d]);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kPrTmemCols);
@@ -286,7 +295,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         fence_proxy_async_smem();  // staged rows -> visible to the TMA engine
         __syncwarp();
         if (lane == 0) {
-          if (y < args.M && gcol < args.N) tma_store_2d(&tmap_out, buf, gcol, y);
+          if (y < args.M && gcol < args.N)
+            for (int d = 0; d < dst.ndst; ++d) tma_store_2d(&dst.m[d], buf, dst.col0 + gcol, y);
           bulk_commit_group();
         }
       }
@@ -297,8 +307,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     }
   }
 
-  // Every tile store has completed before the grid ends.
-  if (warp >= 2 && lane == 0) bulk_wait_group0();
+  // Every tile store has completed (and, for peer destinations, is visible system-wide) before the
+  // grid ends.
+  if (warp >= 2 && lane == 0) {
+    bulk_wait_group0();
+    if (dst.ndst > 1) __threadfence_system();
+  }
   // TMEM is released only after every MMA of the pair has completed and both CTAs are done.
   if (warp == 1) {
     if (lane == 0) mbar_wait(drain_bar, 0, nullptr);
@@ -359,12 +373,13 @@ bool gemm_pair_available() {
   return good;
 }
 
-int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+namespace {
+
+int launch_pair_impl(const uint16_t* a16, const uint16_t* b16, const PairDst& dmaps, int out_dtype, const float* bias,
                      const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act) {
   if (M <= 0 || N <= 0) return G16_OK;
   PairArgs args{};
   args.act = act;
-  args.out = out;
   args.bias = bias;
   args.rscale = rscale;
   args.status = device_status_ptr();
@@ -384,12 +399,6 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
   st = make_tmap_2d(&tb, b16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                     kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
-  // Output: [32 rows x 128 bytes] boxes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
-  CUtensorMap to;
-  const bool f16 = out_dtype == G16_F16;
-  st = make_tmap_2d(&to, out, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, f16 ? 2 : 4,
-                    static_cast<uint64_t>(M), static_cast<uint64_t>(N), 32, f16 ? 64 : 32, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != G16_OK) return st;
   const int max_pairs = dev.sm_count / 2;
   const int pairs = args.units < max_pairs ? args.units : max_pairs;
   cudaLaunchConfig_t cfg{};
@@ -407,14 +416,54 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
   cudaError_t e;
   if (out_dtype == G16_F16) {
     e = ensure_pair_attr(gemm_pair_kernel<true>, g_pair_attr16);
-    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<true>, ta, tb, to, args);
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<true>, ta, tb, dmaps, args);
   } else {
     e = ensure_pair_attr(gemm_pair_kernel<false>, g_pair_attr32);
-    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, to, args);
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, dmaps, args);
   }
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();
   return G16_OK;
+}
+
+}  // namespace
+
+int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act) {
+  if (M <= 0 || N <= 0) return G16_OK;
+  // Output: [32 rows x 128 bytes] boxes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
+  PairDst dmaps{};
+  const bool f16 = out_dtype == G16_F16;
+  int st = make_tmap_2d(&dmaps.m[0], out, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        f16 ? 2 : 4, static_cast<uint64_t>(M), static_cast<uint64_t>(N), 32, f16 ? 64 : 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != G16_OK) return st;
+  dmaps.ndst = 1;
+  dmaps.col0 = 0;
+  return launch_pair_impl(a16, b16, dmaps, out_dtype, bias, rscale, M, K, N, s, dev, act);
+}
+
+int launch_gemm_pair_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
+                             const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
+                             cudaStream_t s, const DeviceInfo& dev) {
+  if (ndst < 1 || ndst > kPrMaxDst) return G16_ERR_ARG;
+  if (M <= 0 || N <= 0) return G16_OK;
+  PairDst dmaps{};
+  const bool f16 = out_dtype == G16_F16;
+  for (int d = 0; d < ndst; ++d) {
+    if (dst[d] == nullptr) return G16_ERR_ARG;
+    // [M, col0 + N] of each destination: columns past this rank's shard are outside the map, so a
+    // partial last box cannot spill into a neighbour's columns.
+    const int st = make_tmap_2d_strided(&dmaps.m[d], dst[d],
+                                        f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                        f16 ? 2 : 4, static_cast<uint64_t>(M),
+                                        static_cast<uint64_t>(col0) + static_cast<uint64_t>(N),
+                                        static_cast<uint64_t>(ldc), 32, f16 ? 64 : 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != G16_OK) return st;
+  }
+  dmaps.ndst = ndst;
+  dmaps.col0 = col0;
+  return launch_pair_impl(a16, b16, dmaps, out_dtype, bias, rscale, M, K, N, s, dev, G16_ACT_NONE);
 }
 
 }  // namespace g16

@@ -59,6 +59,11 @@ int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
 int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                      const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act = 0);
 bool gemm_pair_available();
+// The same kernel storing every output tile into ndst buffers [M, ldc] at column col0 (TMA tile
+// stores; peer buffers for the multi-GPU exchange).
+int launch_gemm_pair_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
+                             const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
+                             cudaStream_t s, const DeviceInfo& dev);
 
 // Medium-M GEMM (g16_gemm_midm.cu): M <= kMidMaxM activation rows, operands swapped so the
 // weight columns are the MMA's M and the rows its N; K split over a cluster, reduced in DSMEM.

@@ -151,10 +151,13 @@ int g16_skinny_plan(int M, int K, int N, int x_dtype, int* info);
 #define G16_SCATTER_MAX_DST 8
 /* flags: how the tiles reach the destinations. G16_SCATTER_DEFAULT picks the measured best;
  * G16_SCATTER_STORES: 16-byte stores by the epilogue warps; G16_SCATTER_TMA: one TMA tile store
- * (cp.async.bulk.tensor, shared -> global) per destination from the staged rows. */
+ * (cp.async.bulk.tensor, shared -> global) per destination from the staged rows; G16_SCATTER_PAIRS:
+ * the CTA-pair kernel (256 x 256 tiles on two SMs) with the same TMA tile stores (falls back to
+ * G16_SCATTER_TMA where a pair cluster cannot be resident). All give the same bits. */
 #define G16_SCATTER_DEFAULT 0
 #define G16_SCATTER_STORES 1
 #define G16_SCATTER_TMA 2
+#define G16_SCATTER_PAIRS 3
 int g16_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
                      const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
                      int flags, void* stream);

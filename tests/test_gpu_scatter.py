@@ -30,7 +30,7 @@ def _gemm_ksplit1(a, b, bias, out_dtype):
                                              (2048, 256, 5120, 6144, 1024)])  # last: split tail
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 @pytest.mark.parametrize("with_bias", [False, True])
-@pytest.mark.parametrize("flags", [0, 1, 2])
+@pytest.mark.parametrize("flags", [0, 1, 2, 3])
 def test_scatter_matches_gemm(cuda_ok, M, K, N, ldc, col0, out_dtype, with_bias, flags):
     gen = torch.Generator(device="cuda").manual_seed(M + N + col0)
     a = torch.randn(M, K, device="cuda", generator=gen).half()
@@ -66,4 +66,4 @@ def test_scatter_rejects_bad_arguments(cuda_ok):
         _native.ERR_UNSUPPORTED
     mis = (ctypes.c_void_p * 1)(d.data_ptr() + 8)
     assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), mis, 1, f16, None, None, 256, 64, 64, 128, 0, 0, s) == _native.ERR_ALIGN
-    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 0, 3, s) == _native.ERR_ARG
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 0, 4, s) == _native.ERR_ARG
