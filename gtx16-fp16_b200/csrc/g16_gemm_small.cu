@@ -93,7 +93,10 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if (static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) >
       dynamic_smem_bytes()) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicExch(args.status, G16_ERR_ARG);
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {
+      grid_dependency_wait();
+      atomicExch(args.status, G16_ERR_ARG);
+    }
     return;
   }
 
@@ -109,6 +112,9 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   const int rpo = (kBM + csize - 1) / csize;                      // rows each rank finalises
   const int own0 = rank * rpo;
   const int own_rows = max(0, min(kBM - own0, rpo));
+  // The next kernel may start its set-up now; it reads nothing this one writes before its own
+  // grid dependency wait.
+  if (threadIdx.x == 0) grid_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSmStages; ++s) {
@@ -135,6 +141,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     if (lane == 0) {
       tma_prefetch_desc(&tmap_a);
       tma_prefetch_desc(&tmap_b);
+      grid_dependency_wait();  // A, B: possibly written by the preceding kernel
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed = 0, armed_phase = 0;
@@ -197,6 +204,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
     const int r_local = quarter * 32 + lane;      // tile row of this lane
     const int row = mt * kBM + r_local;
+    grid_dependency_wait();  // bias, rscale, out
     bool got = mbar_wait(done_bar, 0, abort_flag);
     got = __all_sync(0xffffffffu, got);
     if (!got && lane == 0) {
@@ -335,13 +343,16 @@ int launch_small_t(const uint16_t* a16, const uint16_t* b16, void* out, const fl
   cfg.blockDim = dim3(kSmThreads, 1, 1);
   cfg.dynamicSmemBytes = SmallGeo<BN>::kSmemBytes;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch: a launch's set-up overlaps the previous kernel's tail.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, args);
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();
