@@ -285,8 +285,9 @@ int g16_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst,
                      int flags, void* stream) {
   if (dst == nullptr || ndst < 1 || ndst > G16_SCATTER_MAX_DST) return G16_ERR_ARG;
   if (flags != G16_SCATTER_DEFAULT && flags != G16_SCATTER_STORES && flags != G16_SCATTER_TMA &&
-      flags != G16_SCATTER_PAIRS)
+      flags != G16_SCATTER_PAIRS && flags != G16_SCATTER_MULTIMEM)
     return G16_ERR_ARG;
+  if (flags == G16_SCATTER_MULTIMEM && ndst != 1) return G16_ERR_ARG;
   if (M < 0 || K <= 0 || N < 0 || col0 < 0 || ldc < static_cast<long long>(col0) + N) return G16_ERR_ARG;
   if (out_dtype != G16_F32 && out_dtype != G16_F16) return G16_ERR_ARG;
   if (K % 8 != 0 || N % 8 != 0 || col0 % 8 != 0 || ldc % 8 != 0) return G16_ERR_UNSUPPORTED;

@@ -677,6 +677,11 @@ int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* d
   // Default: CTA pairs. Measured at 2 GPUs (16384^3 N-sharded, interleaved repetitions, median):
   // pairs 3.66 ms per step (the local shard GEMM alone took 3.68 ms: the exchange is hidden),
   // single-CTA 16-byte stores 4.18 ms, single-CTA TMA stores 4.31 ms.
+  if (flags == G16_SCATTER_MULTIMEM) {
+    if (ndst != 1) return G16_ERR_ARG;
+    if (!gemm_pair_available()) return G16_ERR_UNSUPPORTED;
+    return launch_gemm_pair_multimem(a16, b16, dst[0], out_dtype, bias, rscale, M, K, N, ldc, col0, s, dev);
+  }
   if (flags == G16_SCATTER_DEFAULT) flags = G16_SCATTER_PAIRS;
   if (flags == G16_SCATTER_PAIRS) {
     if (gemm_pair_available())

@@ -53,6 +53,10 @@ struct PairDst {
   CUtensorMap m[kPrMaxDst];
   int ndst;
   int col0;
+  // NVLink multicast mode (ndst == 0): the output rows [M, ldc] behind one multicast address; each
+  // 128-byte row segment is written once with multimem.st and reaches every GPU's copy.
+  uint64_t mc;
+  long long ldc;
 };
 
 struct PairArgs {
@@ -156,7 +160,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
-    for (int d = 0; d < dst.ndst; ++d) tma_prefetch_desc(&dst.m[d]);
+    for (int d = 0; d < dst.ndst; ++d) tma_prefetch_desc(&dst.m[d]);  // none in multicast mode
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kPrTmemCols);
@@ -292,12 +296,31 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         // this lane's row: 8 chunks of 16 bytes, swizzled by row (the tensor map's 128-byte swizzle)
 #pragma unroll
         for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = packed[j];
-        fence_proxy_async_smem();  // staged rows -> visible to the TMA engine
-        __syncwarp();
-        if (lane == 0) {
-          if (y < args.M && gcol < args.N)
-            for (int d = 0; d < dst.ndst; ++d) tma_store_2d(&dst.m[d], buf, dst.col0 + gcol, y);
-          bulk_commit_group();
+        if (dst.ndst > 0) {
+          fence_proxy_async_smem();  // staged rows -> visible to the TMA engine
+          __syncwarp();
+          if (lane == 0) {
+            if (y < args.M && gcol < args.N)
+              for (int d = 0; d < dst.ndst; ++d) tma_store_2d(&dst.m[d], buf, dst.col0 + gcol, y);
+            bulk_commit_group();
+          }
+        } else {
+          // Multicast: 8 lanes per 128-byte row segment, 4 rows per instruction, 8 passes.
+          __syncwarp();
+          constexpr int kElems = OUT_F16 ? 8 : 4;  // elements per 16-byte chunk
+          constexpr int kEsz = OUT_F16 ? 2 : 4;
+          const int c = lane & 7;
+          const int col = gcol + c * kElems;  // N % 8 == 0: a chunk is wholly inside or outside
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (lane >> 3);
+            const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 128 + ((c ^ (r & 7)) << 4));
+            const int grow = y + r;
+            if (grow < args.M && col < args.N)
+              multimem_st_v4(dst.mc + (static_cast<uint64_t>(grow) * static_cast<uint64_t>(dst.ldc) +
+                                       static_cast<uint64_t>(dst.col0 + col)) * kEsz, v);
+          }
+          __syncwarp();  // the buffer is read before the next pass rewrites it
         }
       }
       tc_fence_before();
@@ -311,7 +334,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   // grid ends.
   if (warp >= 2 && lane == 0) {
     bulk_wait_group0();
-    if (dst.ndst > 1) __threadfence_system();
+    if (dst.ndst != 1) __threadfence_system();
   }
   // TMEM is released only after every MMA of the pair has completed and both CTAs are done.
   if (warp == 1) {
@@ -441,6 +464,19 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
   dmaps.ndst = 1;
   dmaps.col0 = 0;
   return launch_pair_impl(a16, b16, dmaps, out_dtype, bias, rscale, M, K, N, s, dev, act);
+}
+
+int launch_gemm_pair_multimem(const uint16_t* a16, const uint16_t* b16, void* mc, int out_dtype, const float* bias,
+                              const float* rscale, int M, int K, int N, long long ldc, int col0, cudaStream_t s,
+                              const DeviceInfo& dev) {
+  if (mc == nullptr) return G16_ERR_ARG;
+  if (M <= 0 || N <= 0) return G16_OK;
+  PairDst dmaps{};
+  dmaps.ndst = 0;
+  dmaps.col0 = col0;
+  dmaps.mc = reinterpret_cast<uint64_t>(mc);
+  dmaps.ldc = ldc;
+  return launch_pair_impl(a16, b16, dmaps, out_dtype, bias, rscale, M, K, N, s, dev, G16_ACT_NONE);
 }
 
 int launch_gemm_pair_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,

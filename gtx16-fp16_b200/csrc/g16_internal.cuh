@@ -61,6 +61,11 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
 bool gemm_pair_available();
 // The same kernel storing every output tile into ndst buffers [M, ldc] at column col0 (TMA tile
 // stores; peer buffers for the multi-GPU exchange).
+// The same with every tile written once through an NVLink multicast address covering all ranks'
+// [M, ldc] outputs (multimem.st; the switch replicates it).
+int launch_gemm_pair_multimem(const uint16_t* a16, const uint16_t* b16, void* mc, int out_dtype, const float* bias,
+                              const float* rscale, int M, int K, int N, long long ldc, int col0, cudaStream_t s,
+                              const DeviceInfo& dev);
 int launch_gemm_pair_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
                              const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
                              cudaStream_t s, const DeviceInfo& dev);

@@ -412,6 +412,15 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
       : "memory");
 }
 
+// 16-byte store through an NVLink multicast (NVLS) address: the switch writes it into every GPU's
+// copy of the buffer. The four words are stored bit for bit.
+__device__ __forceinline__ void multimem_st_v4(uint64_t mc_addr, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
+
 // Streaming 128-bit global load that does not allocate in L1 (weights are read exactly once).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;

@@ -27,7 +27,7 @@ _lock = threading.Lock()
 _P, _I, _F, _Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
 IPC_HANDLE_BYTES = 64       # G16_IPC_HANDLE_BYTES
 SCATTER_MAX_DST = 8         # G16_SCATTER_MAX_DST
-SCATTER_DEFAULT, SCATTER_STORES, SCATTER_TMA, SCATTER_PAIRS = 0, 1, 2, 3  # G16_SCATTER_* store methods
+SCATTER_DEFAULT, SCATTER_STORES, SCATTER_TMA, SCATTER_PAIRS, SCATTER_MULTIMEM = 0, 1, 2, 3, 4  # G16_SCATTER_*
 ACT_NONE, ACT_GELU = 0, 1   # G16_ACT_*: activation applied by the GEMM epilogue (g16_mm_t_act)
 SIGNATURES = {
     "g16_mm_t": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),

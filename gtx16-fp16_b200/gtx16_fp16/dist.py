@@ -5,10 +5,12 @@ shapes that shard naturally:
 
 * ``ShardedMatmul``: out[M, N] = a[M, K] @ w_t[K, N] with w_t split by columns. Rank r keeps its
   column shard w_t[:, n_r0:n_r1] resident and computes out[:, n_r0:n_r1]. On CUDA with NCCL and
-  fp16 activations the exchange is fused into the GEMM: the epilogue stores every output tile
-  into each rank's full output buffer (``PeerBuffer``: CUDA IPC mappings over NVLink), so the
-  all-gather overlaps the math and no separate copy pass is needed; two one-element all-reduces
-  per call order the buffers' reuse. Otherwise (fp32 activations, M <= 8, gloo) the shards are
+  fp16 activations the exchange is fused into the GEMM: where the GPUs support NVLink multicast
+  (NVLS) the epilogue writes every output tile once through a multicast address bound to all
+  ranks' output buffers (``MulticastBuffer``: torch symmetric memory) and the switch delivers it
+  everywhere; otherwise it stores every tile into each rank's full output buffer (``PeerBuffer``:
+  CUDA IPC mappings over NVLink). Either way the all-gather overlaps the math and no separate
+  copy pass is needed; two one-element all-reduces per call order the buffers' reuse. Otherwise (fp32 activations, M <= 8, gloo) the shards are
   computed with ``mm_t`` and exchanged with one NCCL all-gather. Every rank ends with the full
   output. Shard boundaries are multiples of 8 columns (the kernels' N % 8 rule).
 * ``batch_slice``: data parallelism over a batch of independent inputs (model inference): rank r
@@ -108,6 +110,40 @@ class PeerBuffer:
         self.tensor = None
 
 
+class MulticastBuffer:
+    """A [rows, cols] buffer on every rank of `group` in torch symmetric memory, with the NVLink
+    multicast address (``mc_ptr``, 0 when the GPUs have no multicast support) that writes all ranks'
+    copies at once. Collective construction; ``close()`` is collective too."""
+
+    def __init__(self, shape: tuple, dtype: torch.dtype, device: torch.device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.group = group if group is not None else dist.group.WORLD
+        self.shape, self.dtype = tuple(shape), dtype
+        self.tensor = symm_mem.empty(*self.shape, dtype=dtype, device=device)
+        self._handle = symm_mem.rendezvous(self.tensor, self.group)
+        self.mc_ptr = int(self._handle.multicast_ptr) if self._handle.multicast_ptr else 0
+
+    @staticmethod
+    def supported(device: torch.device) -> bool:
+        """Whether this GPU can use NVLink multicast through torch symmetric memory."""
+        if device.type != "cuda":
+            return False
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            return bool(symm_mem._SymmetricMemory.has_multicast_support(symm_mem.DeviceType.CUDA,
+                                                                        device.index or 0))
+        except (ImportError, AttributeError, RuntimeError):
+            return False
+
+    def close(self):
+        if self.tensor is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no peer writes into this buffer any more
+        self._handle = None
+        self.tensor = None
+
+
 @dataclass
 class ShardedMatmul:
     """Column-sharded matmul with an all-gather of the output shards.
@@ -126,6 +162,7 @@ class ShardedMatmul:
     local_mm: object = None
     fused: bool | None = None  # None: the fused exchange whenever it applies (see the module doc)
     scatter_flags: int = 0     # G16_SCATTER_* store method of the fused path (0: the library's default)
+    multicast: bool | None = None  # NVLink multicast exchange: None = where supported, False = never
     _bufs: dict = field(default_factory=dict, repr=False)
 
     def __post_init__(self):
@@ -161,14 +198,29 @@ class ShardedMatmul:
         M, K = a.shape
         buf = self._bufs.get(M)
         if buf is None:
-            buf = self._bufs[M] = PeerBuffer((M, self.n_total), self.out_dtype, a.device, self.group)
+            buf = None
+            if self.multicast is not False and MulticastBuffer.supported(a.device):
+                buf = MulticastBuffer((M, self.n_total), self.out_dtype, a.device, self.group)
+                ok = torch.tensor([1 if buf.mc_ptr else 0], dtype=torch.int32, device=a.device)
+                dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+                if not ok.item():  # every rank takes the same path
+                    buf.close()
+                    buf = None
+            if buf is None:
+                if self.multicast:
+                    raise RuntimeError("ShardedMatmul(multicast=True): no NVLink multicast on this group")
+                buf = PeerBuffer((M, self.n_total), self.out_dtype, a.device, self.group)
+            self._bufs[M] = buf
             self._flag = torch.zeros(1, dtype=torch.int32, device=a.device)
         # Peers are done with their outputs of the previous call before any tile lands there.
         dist.all_reduce(self._flag, group=self.group)
-        ptrs = (ctypes.c_void_p * self.world)(*buf.ptrs)
+        if isinstance(buf, MulticastBuffer):
+            ptrs, ndst, flags = (ctypes.c_void_p * 1)(buf.mc_ptr), 1, _native.SCATTER_MULTIMEM
+        else:
+            ptrs, ndst, flags = (ctypes.c_void_p * self.world)(*buf.ptrs), self.world, self.scatter_flags
         st = _native.lib().g16_gemm_scatter(
-            a.data_ptr(), self.w_shard.data_ptr(), ptrs, self.world, _native.dtype_code(self.out_dtype), None,
-            None, M, K, self.n1 - self.n0, self.n_total, self.n0, self.scatter_flags,
+            a.data_ptr(), self.w_shard.data_ptr(), ptrs, ndst, _native.dtype_code(self.out_dtype), None,
+            None, M, K, self.n1 - self.n0, self.n_total, self.n0, flags,
             _native.stream_handle(a.device.index or 0))
         _native.check(st, "g16_gemm_scatter")
         # Every peer's kernel (and so every tile it stored here) has completed.

@@ -153,11 +153,17 @@ int g16_skinny_plan(int M, int K, int N, int x_dtype, int* info);
  * G16_SCATTER_STORES: 16-byte stores by the epilogue warps; G16_SCATTER_TMA: one TMA tile store
  * (cp.async.bulk.tensor, shared -> global) per destination from the staged rows; G16_SCATTER_PAIRS:
  * the CTA-pair kernel (256 x 256 tiles on two SMs) with the same TMA tile stores (falls back to
- * G16_SCATTER_TMA where a pair cluster cannot be resident). All give the same bits. */
+ * G16_SCATTER_TMA where a pair cluster cannot be resident); G16_SCATTER_MULTIMEM: ndst must be 1
+ * and dst[0] an NVLink multicast (NVLS) address bound to every rank's [.., ldc] output buffer (e.g.
+ * torch symmetric memory's multicast_ptr): the CTA-pair kernel writes each 128-byte row segment
+ * once with multimem.st and the switch delivers it to every GPU (G16_ERR_UNSUPPORTED where a pair
+ * cluster cannot be resident; any other address in dst[0] is the caller's error and undefined, as
+ * the library cannot tell a multicast address from another). All give the same bits. */
 #define G16_SCATTER_DEFAULT 0
 #define G16_SCATTER_STORES 1
 #define G16_SCATTER_TMA 2
 #define G16_SCATTER_PAIRS 3
+#define G16_SCATTER_MULTIMEM 4
 int g16_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
                      const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
                      int flags, void* stream);

@@ -1,9 +1,11 @@
 """Column-sharded matmul across 2 GPUs (skipped with fewer than 2 GPUs).
 
-Fused path (fp16 activations, M > 8, NCCL): every rank's GEMM epilogue stores its output tiles into
-both ranks' full output buffers (CUDA IPC over NVLink). The result equals, bit for bit, the same
-column shards computed on one GPU with g16_gemm and ksplit = 1 (same kernel, same K order), and the
-fp64 product within the GEMM tolerance; two calls in a row check the ordering of buffer reuse.
+Fused path (fp16 activations, M > 8, NCCL): every rank's GEMM epilogue writes its output tiles into
+both ranks' full output buffers, once through an NVLink multicast address (torch symmetric memory)
+where the GPUs support it, and with stores into each peer's CUDA IPC mapping otherwise (both paths
+are run). The result equals, bit for bit, the same column shards computed on one GPU with g16_gemm
+and ksplit = 1 (same kernel, same K order), and the fp64 product within the GEMM tolerance; two
+calls in a row check the ordering of buffer reuse.
 Gather path (fused=False): mm_t per shard and one NCCL all-gather; equals the single-GPU shards.
 """
 import os
@@ -39,7 +41,7 @@ def _worker(rank, world, port, ret):
     import torch.distributed as dist
 
     import gtx16_fp16 as g
-    from gtx16_fp16.dist import ShardedMatmul, batch_slice, gather_rows, shard_bounds
+    from gtx16_fp16.dist import MulticastBuffer, ShardedMatmul, batch_slice, gather_rows, shard_bounds
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -47,22 +49,27 @@ def _worker(rank, world, port, ret):
                             device_id=torch.device("cuda", rank))
     results = {}
     try:
-        for M, K, N, out_dtype in ((1024, 2048, 4096, torch.float16), (1000, 1024, 4104, torch.float32)):
-            gen = torch.Generator(device="cuda").manual_seed(M + N)
-            w = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
-            n0, n1 = shard_bounds(N, world, rank)
-            fused = ShardedMatmul(w[:, n0:n1].contiguous(), N, out_dtype=out_dtype)
-            for call in range(2):
-                a = torch.randn(M, K, device="cuda", generator=gen).half()
-                assert fused.fused_applies(a)
-                y = fused(a).clone()
-                shards = [_shard_gemm_ksplit1(a, w[:, b0:b1].contiguous(), out_dtype)
-                          for b0, b1 in (shard_bounds(N, world, r) for r in range(world))]
-                ref = a.double() @ w.double()
-                results[f"fused {M}x{K}x{N} {out_dtype} call {call} bitwise"] = torch.equal(y, torch.cat(shards, dim=1))
-                results[f"fused {M}x{K}x{N} {out_dtype} call {call} fp64"] = \
-                    ((y.double() - ref).norm() / ref.norm()).item() < 1e-3
-            fused.close()
+        for mc in (None, False):  # None: NVLink multicast where supported; False: peer stores
+            for M, K, N, out_dtype in ((1024, 2048, 4096, torch.float16), (1000, 1024, 4104, torch.float32)):
+                gen = torch.Generator(device="cuda").manual_seed(M + N)
+                w = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
+                n0, n1 = shard_bounds(N, world, rank)
+                fused = ShardedMatmul(w[:, n0:n1].contiguous(), N, out_dtype=out_dtype, multicast=mc)
+                tag = f"{'peer' if mc is False else 'auto'} {M}x{K}x{N} {out_dtype}"
+                for call in range(2):
+                    a = torch.randn(M, K, device="cuda", generator=gen).half()
+                    assert fused.fused_applies(a)
+                    y = fused(a).clone()
+                    shards = [_shard_gemm_ksplit1(a, w[:, b0:b1].contiguous(), out_dtype)
+                              for b0, b1 in (shard_bounds(N, world, r) for r in range(world))]
+                    ref = a.double() @ w.double()
+                    results[f"fused {tag} call {call} bitwise"] = torch.equal(y, torch.cat(shards, dim=1))
+                    results[f"fused {tag} call {call} fp64"] = ((y.double() - ref).norm() / ref.norm()).item() < 1e-3
+                if mc is False:
+                    results[f"fused {tag} took the peer path"] = not isinstance(fused._bufs[M], MulticastBuffer)
+                else:
+                    ret[f"multicast {rank}"] = isinstance(fused._bufs[M], MulticastBuffer)
+                fused.close()
         # gather path (mm_t per shard + NCCL all-gather)
         gen = torch.Generator(device="cuda").manual_seed(0)
         M, K, N = 1024, 2048, 4096
@@ -88,7 +95,8 @@ def test_sharded_matmul_two_gpus():
     import torch.multiprocessing as mp
     ret = mp.Manager().dict()
     mp.spawn(_worker, args=(2, _free_port(), ret), nprocs=2, join=True)
-    got = dict(ret)
+    got = {k: v for k, v in dict(ret).items() if isinstance(k, int)}
+    print("multicast path used:", {k: v for k, v in dict(ret).items() if not isinstance(k, int)})
     assert sorted(got) == [0, 1]
     for rank, res in got.items():
         bad = [k for k, v in res.items() if not v]

@@ -66,4 +66,6 @@ def test_scatter_rejects_bad_arguments(cuda_ok):
         _native.ERR_UNSUPPORTED
     mis = (ctypes.c_void_p * 1)(d.data_ptr() + 8)
     assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), mis, 1, f16, None, None, 256, 64, 64, 128, 0, 0, s) == _native.ERR_ALIGN
-    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 0, 4, s) == _native.ERR_ARG
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), one, 1, f16, None, None, 256, 64, 64, 128, 0, 5, s) == _native.ERR_ARG
+    two = (ctypes.c_void_p * 2)(d.data_ptr(), d.data_ptr())  # multicast mode takes exactly one address
+    assert L.g16_gemm_scatter(a.data_ptr(), b.data_ptr(), two, 2, f16, None, None, 256, 64, 64, 128, 0, 4, s) == _native.ERR_ARG
