@@ -871,8 +871,9 @@ def main():
         return  # the reference arm is the host CPU path: rank 0 alone runs and prints it
     if world > 1 and args.impl == "ours":
         import torch.distributed as dist
-        # The only collectives are small (barrier all-reduces, result gathers): no NVLink multicast
-        # objects are needed, and none stay bound to a rank's memory.
+        # NCCL's own collectives are small (barrier all-reduces, result gathers), so NCCL runs without
+        # NVLS; the sharded GEMM's exchange binds its output to a multicast object of its own
+        # (torch symmetric memory) where the GPUs support it.
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
