@@ -302,11 +302,13 @@ class ShardedGemm(Workload):
     every rank. Total work is fixed: strong scaling."""
     bound = "tensor"
     graphable = False
+    multicast = None  # ShardedMatmul.multicast: None = NVLink multicast where supported, False = peer stores
 
     def __init__(self, dev, world, rank, M=16384, K=16384, N=16384):
         super().__init__(dev)
         from gtx16_fp16.dist import ShardedMatmul, shard_bounds
         self.M, self.K, self.N, self.world, self.rank = M, K, N, world, rank
+        self._exchange = None
         self.name = "gemm16384"
         self.metric = f"GEMM TFLOPS (fp16 {M}x{K}x{N}, N-sharded over GPUs, all-gather fused into the epilogue)"
         self.unit = "TFLOPS"
@@ -323,11 +325,12 @@ class ShardedGemm(Workload):
                 b[:, lo - n0:hi - n0] = panel[:, lo - c0:hi - c0]
             del panel
         self.B = b
-        self.sm = ShardedMatmul(self.B, N, out_dtype=torch.float16)
+        self.sm = ShardedMatmul(self.B, N, out_dtype=torch.float16, multicast=self.multicast)
 
     def config(self):
         return {"workload": self.name, "M": self.M, "K": self.K, "N": self.N, "in": "fp16", "out": "fp16",
                 "shard": f"w_t columns [{self.sm.n0}, {self.sm.n1}) on rank {self.rank}",
+                "exchange": self._exchange or self.exchange(),
                 "inputs": "A~N(0,1), B~N(0,1/sqrt(K)) fp16, seed 0 (BASELINE config 3)",
                 "l2": "A alone is 512 MiB > 126 MB L2"}
 
@@ -343,7 +346,18 @@ class ShardedGemm(Workload):
     def local_step(self, g16):
         return self.sm.local(self.A)
 
+    def exchange(self):
+        from gtx16_fp16.dist import MulticastBuffer
+        if self.world == 1:
+            return "none (one rank)"
+        bufs = list(self.sm._bufs.values())
+        if not bufs:
+            return "not run"
+        return ("NVLink multicast stores (multimem.st) from the GEMM epilogue"
+                if isinstance(bufs[0], MulticastBuffer) else "peer TMA stores from the GEMM epilogue (CUDA IPC)")
+
     def close(self):
+        self._exchange = self.exchange()
         self.sm.close()
 
     def host_inputs(self):
@@ -861,7 +875,10 @@ def main():
                     help="comma list of other workloads measured briefly into 'sub' (rank 0); '' to skip")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graph", type=int, default=1, help="1: time a CUDA graph of the K steps (default); 0: eager")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "peer"],
+                    help="gemm16384 on N > 1 GPUs: NVLink multicast where supported (auto) or peer stores")
     args = ap.parse_args()
+    ShardedGemm.multicast = None if args.exchange == "auto" else False
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
