@@ -198,18 +198,7 @@ class ShardedMatmul:
         M, K = a.shape
         buf = self._bufs.get(M)
         if buf is None:
-            buf = None
-            if self.multicast is not False and MulticastBuffer.supported(a.device):
-                buf = MulticastBuffer((M, self.n_total), self.out_dtype, a.device, self.group)
-                ok = torch.tensor([1 if buf.mc_ptr else 0], dtype=torch.int32, device=a.device)
-                dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
-                if not ok.item():  # every rank takes the same path
-                    buf.close()
-                    buf = None
-            if buf is None:
-                if self.multicast:
-                    raise RuntimeError("ShardedMatmul(multicast=True): no NVLink multicast on this group")
-                buf = PeerBuffer((M, self.n_total), self.out_dtype, a.device, self.group)
+            buf = self._exchange_buffer(M, a.device)
             self._bufs[M] = buf
             self._flag = torch.zeros(1, dtype=torch.int32, device=a.device)
         # Peers are done with their outputs of the previous call before any tile lands there.
@@ -229,6 +218,28 @@ class ShardedMatmul:
             out.copy_(buf.tensor)
             return out
         return buf.tensor
+
+    def _exchange_buffer(self, M: int, device: torch.device):
+        """The output buffer of the fused path for M rows (collective). A MulticastBuffer where
+        every rank built one with a multicast address, else a PeerBuffer: the ranks agree with one
+        MIN all-reduce and then take the same path, so a rank whose multicast set-up failed does not
+        leave its peers waiting in a different collective."""
+        if self.multicast is not False and MulticastBuffer.supported(device):
+            try:
+                buf = MulticastBuffer((M, self.n_total), self.out_dtype, device, self.group)
+            except RuntimeError:
+                buf = None
+            ok = torch.tensor([1 if buf is not None and buf.mc_ptr else 0], dtype=torch.int32, device=device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+            if ok.item():
+                return buf
+            if buf is not None:
+                buf.close()  # one barrier, like the bare barrier of the ranks without a buffer
+            else:
+                dist.barrier(group=self.group)
+        if self.multicast:
+            raise RuntimeError("ShardedMatmul(multicast=True): no NVLink multicast on this group")
+        return PeerBuffer((M, self.n_total), self.out_dtype, device, self.group)
 
     def close(self):
         """Release the fused path's peer buffers (collective: every rank calls it)."""

@@ -72,3 +72,65 @@ def test_sharded_matmul_gloo_world2(n_total):
     ret = mp.Manager().dict()
     mp.spawn(_worker, args=(world, _free_port(), n_total, ret), nprocs=world, join=True)
     assert dict(ret) == {0: True, 1: True}
+
+
+class _FakeMulticast:
+    """Stands in for dist.MulticastBuffer on gloo ranks: construction fails on the ranks listed in
+    `fail`, otherwise it yields a buffer with a multicast address; close() is collective."""
+    fail = ()
+    closed = 0
+
+    def __init__(self, shape, dtype, device, group=None):
+        if dist.get_rank() in self.fail:
+            raise RuntimeError("multicast object could not be created")
+        self.mc_ptr = 1
+        self.group = group
+
+    @staticmethod
+    def supported(device):
+        return True
+
+    def close(self):
+        type(self).closed += 1
+        dist.barrier(group=self.group)
+
+
+class _FakePeer:
+    def __init__(self, shape, dtype, device, group=None):
+        self.shape = shape
+
+
+def _exchange_worker(rank, world, port, fail, multicast, ret):
+    import gtx16_fp16.dist as gdist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _FakeMulticast.fail = fail
+        gdist.MulticastBuffer, gdist.PeerBuffer = _FakeMulticast, _FakePeer
+        sm = ShardedMatmul(torch.zeros(8, 16), 16 * world, out_dtype=torch.float32,
+                           local_mm=lambda x, ws: x @ ws, multicast=multicast)
+        try:
+            buf = sm._exchange_buffer(24, torch.device("cpu"))
+            kind = type(buf).__name__
+        except RuntimeError:
+            kind = "raised"
+        dist.barrier()  # every rank left the agreement with the same collectives
+        ret[rank] = (kind, _FakeMulticast.closed)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail,multicast,want", [
+    ((), None, {0: ("_FakeMulticast", 0), 1: ("_FakeMulticast", 0)}),
+    ((0,), None, {0: ("_FakePeer", 0), 1: ("_FakePeer", 1)}),
+    ((1,), False, {0: ("_FakePeer", 0), 1: ("_FakePeer", 0)}),
+    ((0,), True, {0: ("raised", 0), 1: ("raised", 1)}),
+])
+def test_exchange_buffer_ranks_agree_gloo_world2(fail, multicast, want):
+    """The fused path's buffer choice: one rank's failed multicast set-up sends every rank to peer
+    stores (the rank that built one releases it), multicast=False never tries, multicast=True
+    raises on every rank."""
+    world = 2
+    ret = mp.Manager().dict()
+    mp.spawn(_exchange_worker, args=(world, _free_port(), fail, multicast, ret), nprocs=world, join=True)
+    assert dict(ret) == want
