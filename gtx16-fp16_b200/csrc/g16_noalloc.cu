@@ -6,10 +6,12 @@
 // cudaMalloc/cudaFree on latency-critical threads because those calls can synchronise the device.
 // Such callers cannot provide the workspace that g16_gemm needs for its split-K partial tiles.
 //
-// This variant keeps those partial tiles in one fixed array in device memory instead:
-// g16_static_scratch below, 8 MiB, i.e. at most 64 partial tiles of 128 x 256 fp32. Every GPU that
-// loads this library holds the array until the process exits. Problems whose split-K partials do
-// not fit are rejected with G16_ERR_TOO_LARGE.
+// This variant runs g16_gemm's own plan. Most plans need no scratch at all; the one that does, the
+// split into fp32 partial tiles reduced by a second kernel, keeps those tiles in one fixed array in
+// device memory instead of a workspace: g16_static_scratch below, 8 MiB, i.e. at most 64 partial
+// tiles of 128 x 256 fp32. Every GPU that loads this library holds the array until the process
+// exits. An explicit split whose partials do not fit is rejected with G16_ERR_TOO_LARGE; the
+// automatic plan lowers such a split until they fit.
 //
 // The array is shared by every call on a device and keeps whatever the last call wrote. Nothing in
 // it has to start at zero: each call writes every partial tile it later reads. Two calls whose
@@ -60,6 +62,12 @@ size_t partials_bytes(int M, int K, int N, int ksplit) { return gemm_workspace_b
 
 using namespace g16;
 
+// The plan is g16_gemm's own: launch_gemm is called with the static array as its workspace. Most
+// plans need no workspace at all (the medium-M kernel, the small-problem and in-cluster split
+// kernels, single passes); only the partial-tile split (ksplit > 16, or a split whose cluster
+// cannot be resident) uses the array, and launch_gemm checks that its partials fit before it
+// launches anything (G16_ERR_WORKSPACE, nothing enqueued). So the same arguments give the same
+// kernel and the same bits as g16_gemm whenever the partials fit.
 extern "C" int g16_gemm_static_scratch(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype,
                                        const float* bias, const float* rscale, int M, int K, int N, int ksplit,
                                        void* stream) {
@@ -72,17 +80,17 @@ extern "C" int g16_gemm_static_scratch(const uint16_t* a16, const uint16_t* b16,
   int st = G16_OK;
   const DeviceInfo* dev = device_info(&st);
   if (dev == nullptr) return st;
-  if (ksplit == 0) {
-    // automatic: the usual choice, lowered until the partial tiles fit the static array
-    ksplit = gemm_auto_ksplit(M, K, N, *dev);
-    while (ksplit > 1 && partials_bytes(M, K, N, ksplit) > kStaticScratchBytes) --ksplit;
-  }
-  if (ksplit > 1 && partials_bytes(M, K, N, ksplit) > kStaticScratchBytes) return G16_ERR_TOO_LARGE;
   void* scratch = nullptr;
-  if (ksplit > 1) {
-    st = scratch_address(&scratch);
-    if (st != G16_OK) return st;
+  st = scratch_address(&scratch);
+  if (st != G16_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = launch_gemm(a16, b16, out, out_dtype, bias, rscale, M, K, N, ksplit, scratch, kStaticScratchBytes, s, *dev);
+  if (st == G16_ERR_WORKSPACE && ksplit == 0) {
+    // The automatic plan fell through to the partial-tile split and its partials do not fit:
+    // lower that split until they do (down to a single pass) and run it explicitly.
+    int ks = gemm_auto_ksplit(M, K, N, *dev);
+    while (ks > 1 && partials_bytes(M, K, N, ks) > kStaticScratchBytes) --ks;
+    st = launch_gemm(a16, b16, out, out_dtype, bias, rscale, M, K, N, ks, scratch, kStaticScratchBytes, s, *dev);
   }
-  return launch_gemm(a16, b16, out, out_dtype, bias, rscale, M, K, N, ksplit, scratch,
-                     ksplit > 1 ? kStaticScratchBytes : 0, static_cast<cudaStream_t>(stream), *dev);
+  return st == G16_ERR_WORKSPACE ? G16_ERR_TOO_LARGE : st;
 }

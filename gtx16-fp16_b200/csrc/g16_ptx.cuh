@@ -74,17 +74,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`. Returns false when the limit expires or when another
+// Bounded wait for phase `parity` of `bar`. Returns false when `limit_ns` expires or when another
 // role of the CTA already aborted (abort flag in shared memory is non-zero).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, const volatile int* abort_flag,
+                                                uint64_t limit_ns) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
     if (abort_flag != nullptr && *abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
+}
+
+// The wait every pipeline in this library uses: the limit is kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
+  return mbar_wait_limit(bar, parity, abort_flag, kWaitLimitNs);
 }
 
 // Bounded wait with cluster-scope acquire: for a barrier whose transactions are remote st.async

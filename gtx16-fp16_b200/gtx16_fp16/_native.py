@@ -49,6 +49,7 @@ SIGNATURES = {
     "g16_gemm_plan": (_I, [_I, _I, _I, ctypes.POINTER(_I)]),
     "g16_skinny_plan": (_I, [_I, _I, _I, _I, ctypes.POINTER(_I)]),
     "g16_device_status": (_I, [ctypes.POINTER(_I), _I, _P]),
+    "g16_selftest_wait_timeout": (_I, [_I, _P]),
     "g16_launch_count": (ctypes.c_uint64, []),
     "g16_strerror": (ctypes.c_char_p, [_I]),
     "g16_last_cuda_error": (_I, []),

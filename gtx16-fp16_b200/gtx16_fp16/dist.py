@@ -112,14 +112,23 @@ class PeerBuffer:
 
 class MulticastBuffer:
     """A [rows, cols] buffer on every rank of `group` in torch symmetric memory, with the NVLink
-    multicast address (``mc_ptr``, 0 when the GPUs have no multicast support) that writes all ranks'
-    copies at once. Collective construction; ``close()`` is collective too."""
+    multicast address (``mc_ptr``) that writes all ranks' copies at once.
+
+    Set-up has two steps so that callers can agree between them: construction allocates this
+    rank's copy and is local (no collective); ``rendezvous()`` is collective and sets ``mc_ptr``
+    (0 when the group has no multicast object). After a rendezvous ``close()`` is collective; a
+    buffer that never took part in one is dropped with the local ``release()``."""
 
     def __init__(self, shape: tuple, dtype: torch.dtype, device: torch.device, group=None):
         import torch.distributed._symmetric_memory as symm_mem
         self.group = group if group is not None else dist.group.WORLD
         self.shape, self.dtype = tuple(shape), dtype
         self.tensor = symm_mem.empty(*self.shape, dtype=dtype, device=device)
+        self._handle = None
+        self.mc_ptr = 0
+
+    def rendezvous(self):
+        import torch.distributed._symmetric_memory as symm_mem
         self._handle = symm_mem.rendezvous(self.tensor, self.group)
         self.mc_ptr = int(self._handle.multicast_ptr) if self._handle.multicast_ptr else 0
 
@@ -135,13 +144,16 @@ class MulticastBuffer:
         except (ImportError, AttributeError, RuntimeError):
             return False
 
+    def release(self):
+        self._handle = None
+        self.tensor = None
+
     def close(self):
         if self.tensor is None:
             return
         torch.cuda.synchronize()
         dist.barrier(group=self.group)  # no peer writes into this buffer any more
-        self._handle = None
-        self.tensor = None
+        self.release()
 
 
 @dataclass
@@ -220,23 +232,32 @@ class ShardedMatmul:
         return buf.tensor
 
     def _exchange_buffer(self, M: int, device: torch.device):
-        """The output buffer of the fused path for M rows (collective). A MulticastBuffer where
-        every rank built one with a multicast address, else a PeerBuffer: the ranks agree with one
-        MIN all-reduce and then take the same path, so a rank whose multicast set-up failed does not
-        leave its peers waiting in a different collective."""
-        if self.multicast is not False and MulticastBuffer.supported(device):
+        """The output buffer of the fused path for M rows (collective). A MulticastBuffer where every
+        rank can build one with a multicast address, else a PeerBuffer.
+
+        Every step whose outcome can differ between ranks ends in a MIN all-reduce of a success flag,
+        so all ranks take the same collectives and the same buffer: (1) multicast support, a local
+        query; (2) this rank's allocation, local; (3) the rendezvous, a collective, and its multicast
+        address. A rank whose support or allocation failed therefore never leaves its peers waiting
+        inside the rendezvous. (The rendezvous itself cannot be guarded this way: a rank that raises
+        inside it raises on its own.)"""
+        def agree(ok: bool) -> bool:
+            t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.group)
+            return bool(t.item())
+
+        if self.multicast is not False and agree(MulticastBuffer.supported(device)):
             try:
                 buf = MulticastBuffer((M, self.n_total), self.out_dtype, device, self.group)
             except RuntimeError:
                 buf = None
-            ok = torch.tensor([1 if buf is not None and buf.mc_ptr else 0], dtype=torch.int32, device=device)
-            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
-            if ok.item():
-                return buf
-            if buf is not None:
-                buf.close()  # one barrier, like the bare barrier of the ranks without a buffer
-            else:
-                dist.barrier(group=self.group)
+            if agree(buf is not None):
+                buf.rendezvous()
+                if agree(buf.mc_ptr != 0):
+                    return buf
+                buf.close()
+            elif buf is not None:
+                buf.release()
         if self.multicast:
             raise RuntimeError("ShardedMatmul(multicast=True): no NVLink multicast on this group")
         return PeerBuffer((M, self.n_total), self.out_dtype, device, self.group)

@@ -18,16 +18,18 @@ from .ops import SKINNY_MAX_M, is_affected, mm_t, supported
 
 
 class FastLinear(nn.Module):
-    """Inference-only linear layer backed by libg16.
+    """An nn.Linear for inference whose matmuls run in libg16.
 
-    - Weight stored once as fp16, transposed to [in, out] (half the memory of fp32).
-    - Small batches (<= 8 rows, e.g. token-by-token generation) compute in fp32 from fp32 inputs
-      on the HBM-streaming skinny kernel (one C call, no zero-fill).
-    - Larger batches run the tcgen05 tensor-core GEMM: fp32 inputs are cast to fp16 with the per-row
-      power-of-two rescale of rows with |max| > 1024, products accumulate in fp32, and the unscale
-      and fp32 bias are fused into the epilogue.
-    - Output dtype follows the input dtype (fp32 in -> fp32 out).
-    - When autograd is needed or the shape is unsupported, falls back to F.linear (linear.py:45-46,69-70).
+    - The weight is kept once, in fp16 and already transposed: ``weight_t`` is [in, out], so the
+      layer holds half the bytes of an fp32 nn.Linear.
+    - Up to 8 rows of fp32 input (decoding one token at a time, say) go to the skinny GEMV kernel,
+      which multiplies and accumulates in fp32 with one C call and no zero-filled output.
+    - More rows go to the tcgen05 GEMM: fp32 rows are rounded to fp16 (rows above 1024 in magnitude
+      are first divided by a power of two), products accumulate in fp32 and the epilogue undoes the
+      row scale and adds the fp32 bias.
+    - The result has the input's dtype: fp16 in gives fp16 out, fp32 in gives fp32 out.
+    - Inputs that need a gradient, and shapes mm_t does not accept, are computed with F.linear, the
+      reference's own fallback (linear.py:45-46,69-70).
     - ``activation = "gelu"`` (set by ``patch(..., fuse=True)``, not in the reference) applies the
       exact GELU in the GEMM epilogue; a layer in a shared-input group (attention's query/key/value)
       computes the group's fused GEMM once per input and returns its column slice.
@@ -52,7 +54,7 @@ class FastLinear(nn.Module):
         return m
 
     @property
-    def weight(self) -> torch.Tensor:  # some model code reads .weight (e.g. for dtype/device)
+    def weight(self) -> torch.Tensor:  # for callers that inspect .weight (its dtype, device, shape)
         return self.weight_t.t()
 
     def _apply(self, fn, recurse=True):
@@ -98,7 +100,7 @@ class FastLinear(nn.Module):
         x2 = x.reshape(-1, self.in_features)
         if x2.dtype not in (torch.float16, torch.float32):
             x2 = x2.float()
-        x2 = x2.contiguous()  # fp32 stays fp32: the kernels cast (and rescale large rows) themselves
+        x2 = x2.contiguous()  # no cast here: libg16 rounds fp32 rows to fp16 (with the row rescale)
         if x2.shape[0] == 0 or not supported(x2, self.weight_t):
             y = F.linear(x2.float(), self.weight_t.t().float(), self.bias)
             if self.activation == "gelu":
@@ -227,12 +229,14 @@ def _fuse(model: nn.Module) -> tuple[int, int]:
 
 def patch(model: nn.Module, min_features: int = 256, force: bool = False,
           skip: tuple[str, ...] = (), *, activations: torch.dtype | None = None, fuse: bool = False) -> int:
-    """Replace nn.Linear layers in-place with FastLinear. Returns the number replaced.
+    """Swap the model's eligible nn.Linear children for FastLinear copies, in place, and return
+    how many were swapped.
 
-    Same selection rules as the reference (linear.py:79-99): only on affected GPUs unless
-    force=True (B200 is not "affected", so pass force=True there); CUDA weights only; in and out
-    features >= min_features and multiples of 8; qualified names containing any string in `skip`
-    are left alone (e.g. skip=("lm_head",) keeps an output head in fp32).
+    A layer is eligible under the reference's rules (linear.py:79-99): the model has a parameter on
+    an affected GPU, or force=True (a B200 is never affected, so pass force=True there); the layer's
+    weight is on a CUDA device; both feature counts are at least min_features and divisible by 8;
+    and no string in `skip` occurs in its dotted name (skip=("lm_head",), for example, leaves a
+    model's output head as an fp32 nn.Linear).
 
     activations=torch.float16 (opt-in, not in the reference) also converts the rest of the model
     to fp16 after the swap, so activations stay fp16 between layers: each FastLinear then reads

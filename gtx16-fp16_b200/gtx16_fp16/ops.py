@@ -19,22 +19,23 @@ import torch
 from . import _native
 from ._native import G16Error, dtype_code, stream_handle
 
-# TU116 / TU117 device-name pattern, kept verbatim in meaning from ops.py:11.
+# Device names of the tensor-core-less Turing parts the reference targets (the same pattern as
+# its ops.py:11, so is_affected answers the same on every device name).
 _AFFECTED = re.compile(r"GTX 16\d\d|MX ?450|MX ?550|\bT400\b|\bT600\b|\bT1000\b|T1200", re.I)
-_sms: dict[int, int] = {}
 
-# Rows whose |max| exceeds this are scaled down by a power of two before the fp16 cast (GEMM path).
+# GEMM path only: an fp32 activation row whose largest magnitude is above this value is divided by
+# a power of two before it is rounded to fp16, and the product is multiplied back in the epilogue.
 ROW_SCALE_THRESHOLD = 1024.0
-# Largest M served by the skinny (HBM-streaming GEMV) path.
+# Activations with at most this many rows take the HBM-streaming GEMV kernel instead of the GEMM.
 SKINNY_MAX_M = 8
 
 _ws_cache: dict[tuple[int, int, int, int, int], int] = {}
 
 
 def is_affected(device: torch.device | int | None = None) -> bool:
-    """True when the device is a Turing GPU without tensor cores (cc 7.5, TU116/TU117).
-
-    Unchanged from the reference: it is False on B200, so ``patch`` needs ``force=True`` there."""
+    """Whether ``device`` (default: the current one) is one of the cc 7.5 GTX 16xx-class parts the
+    reference was written for. Same answer as the reference for every device; on a B200 it is
+    False, which is why ``patch`` is called with ``force=True`` there."""
     if not torch.cuda.is_available():
         return False
     idx = torch.cuda.current_device() if device is None else torch.device(device).index or 0
@@ -44,19 +45,13 @@ def is_affected(device: torch.device | int | None = None) -> bool:
 
 
 def supported(x2d: torch.Tensor, w_t: torch.Tensor) -> bool:
-    """x2d: [M, K] fp16/fp32 contiguous CUDA; w_t: [K, N] fp16 contiguous, 16-byte aligned;
-    K % 8 == 0 and N % 8 == 0 (the reference's gate, ops.py:29-35)."""
+    """Whether mm_t accepts this pair: a 2-D contiguous CUDA activation in fp16 or fp32 whose
+    width equals the weight's K, and a contiguous fp16 weight [K, N] starting on a 16-byte boundary,
+    with both K and N multiples of 8. The predicate is the reference's (ops.py:29-35) term for term."""
     K, N = w_t.shape
     return (x2d.is_cuda and x2d.dim() == 2 and x2d.dtype in (torch.float16, torch.float32)
             and w_t.dtype == torch.float16 and x2d.is_contiguous() and w_t.is_contiguous()
             and x2d.shape[1] == K and K % 8 == 0 and N % 8 == 0 and w_t.data_ptr() % 16 == 0)
-
-
-def _sm_count(device: torch.device) -> int:
-    i = device.index or 0
-    if i not in _sms:
-        _sms[i] = torch.cuda.get_device_properties(i).multi_processor_count
-    return _sms[i]
 
 
 def skinny_config(N: int, K: int, sms: int) -> tuple[tuple[int, int, int], int]:
@@ -138,8 +133,9 @@ def _mm_t_launch(lib, x, w_t, b, out, xcode, M, K, N, dev, idx, act=_native.ACT_
 
 
 def matmul(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
-    """Drop-in for a @ b with 2-D fp16 inputs. Falls back to torch.matmul when the shape is not
-    supported (the reference's documented behaviour). Default output dtype: fp16 (same as torch)."""
+    """a @ b for two 2-D fp16 CUDA matrices on libg16's tensor-core GEMM, fp16 result unless
+    ``out_dtype`` says otherwise. Anything mm_t does not accept (CPU tensors, other dtypes or ranks,
+    K or N not a multiple of 8) is computed by torch.matmul and cast, as in the reference (ops.py:119)."""
     out_dtype = out_dtype or torch.float16
     if a.dim() == 2 and b.dim() == 2 and a.dtype == b.dtype == torch.float16 and a.is_cuda:
         a_c, b_c = a.contiguous(), b.contiguous()

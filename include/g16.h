@@ -118,13 +118,17 @@ int g16_gemm_auto_ksplit(int M, int K, int N);
  * No counterpart in the reference: an entry point for callers that cannot allocate device memory
  * at call time (e.g. servers that reserve all GPU memory for their own pools at start-up, or hosts
  * that keep cudaMalloc/cudaFree, which can synchronise the device, off latency-critical threads).
- * Same operation and arguments as g16_gemm without a workspace: split-K partial tiles go to a fixed
- * array in device memory of G16_STATIC_SCRATCH_BYTES (8 MiB, 64 partial tiles of 128 x 256 fp32),
- * held by every GPU that loads the library until exit. Problems whose partials do not fit return
- * G16_ERR_TOO_LARGE; ksplit = 0 picks the usual split, lowered until it fits. Allocates nothing.
- * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture. All calls on a device share the
- * array: nothing in it needs to start at zero, but calls that overlap on the GPU race on it.
+ * Same operation, arguments and launch plan as g16_gemm without a workspace: the plans that need
+ * none (medium-M, small-problem and in-cluster split kernels, single passes) run as they do there;
+ * the partial-tile split (ksplit > 16, or a split whose cluster cannot be resident) keeps its fp32
+ * partial tiles in a fixed array in device memory of G16_STATIC_SCRATCH_BYTES (8 MiB, 64 partial
+ * tiles of 128 x 256), held by every GPU that loads the library until exit. An explicit split
+ * whose partials do not fit returns G16_ERR_TOO_LARGE with nothing launched; with ksplit = 0 such
+ * a split is lowered until its partials fit (only then can the bits differ from g16_gemm's).
+ * Allocates nothing. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.
+ * All calls on a device share the array: nothing in it needs to start at zero, but calls that
+ * overlap on the GPU race on it.
  */
 #define G16_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
 int g16_gemm_static_scratch(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
@@ -194,6 +198,15 @@ int g16_gemm_plan(int M, int K, int N, int* info);
 /* Device-side status word of the current device: G16_OK, or G16_ERR_TIMEOUT if a kernel's
  * bounded wait expired since the last clear. Synchronises `stream`. clear != 0 resets it. */
 int g16_device_status(int* status_out, int clear, void* stream);
+
+/* No counterpart in the reference (its failure surface is the launch error of kernels.py:300-302):
+ * a failure-detection self-test. Launches one small kernel whose bounded device-side waits run out
+ * on purpose: one role waits limit_us microseconds (1 .. 1,000,000) on an mbarrier nothing arrives
+ * on, then records G16_ERR_TIMEOUT in the device status word and raises its CTA's abort flag; a
+ * second role, waiting with the library's full 1 s limit, leaves as soon as it sees the flag. No
+ * fault, no trap, no hang: the kernel ends shortly after limit_us and the context stays usable.
+ * Read (and clear) the result with g16_device_status. Returns G16_ERR_ARG for limit_us out of range. */
+int g16_selftest_wait_timeout(int limit_us, void* stream);
 
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t g16_launch_count(void);

@@ -8,7 +8,8 @@ oracle/ref_launch.cu (launchers restating the reference's host dispatch) with th
 sm_100a, and deletes the temporary copy. Only the built library is kept, under oracle/_ref/ (ignored
 by git). The GPU box never reads the reference checkout; it loads the prebuilt library.
 
-Usage: python oracle/build_ref.py [--reference /path/to/reference]
+Usage: python oracle/build_ref.py --reference <reference checkout>
+       (or set G16_REFERENCE_DIR; there is no default location)
 """
 from __future__ import annotations
 
@@ -23,7 +24,12 @@ import tempfile
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 OUT = os.path.join(OUT_DIR, "libg16ref_gpu.so")
-DEFAULT_REF = "/root/reference"
+ENV_VAR = "G16_REFERENCE_DIR"
+
+
+def reference_dir(explicit: str | None = None) -> str | None:
+    """The reference checkout: `explicit`, else $G16_REFERENCE_DIR, else None."""
+    return explicit or os.environ.get(ENV_VAR) or None
 
 
 def extract_src(kernels_py: str) -> str:
@@ -36,11 +42,13 @@ def extract_src(kernels_py: str) -> str:
     raise RuntimeError(f"_SRC string not found in {kernels_py}")
 
 
-def build(reference: str = DEFAULT_REF, quiet: bool = False) -> str | None:
-    kernels_py = os.path.join(reference, "src", "gtx16_fp16", "kernels.py")
-    if not os.path.exists(kernels_py):
+def build(reference: str | None = None, quiet: bool = False) -> str | None:
+    reference = reference_dir(reference)
+    kernels_py = os.path.join(reference, "src", "gtx16_fp16", "kernels.py") if reference else ""
+    if not kernels_py or not os.path.exists(kernels_py):
         if not quiet:
-            print(f"build_ref: {kernels_py} not found; skipping (prebuilt {OUT} is used if present)")
+            print(f"build_ref: no reference checkout ({kernels_py or 'none given'}); skipping "
+                  f"(prebuilt {OUT} is used if present)")
         return OUT if os.path.exists(OUT) else None
     src = extract_src(kernels_py)
     os.makedirs(OUT_DIR, exist_ok=True)
@@ -60,8 +68,10 @@ def build(reference: str = DEFAULT_REF, quiet: bool = False) -> str | None:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REF)
+    ap.add_argument("--reference", default=None, help=f"reference checkout (else ${ENV_VAR})")
     a = ap.parse_args()
+    if reference_dir(a.reference) is None:
+        ap.error(f"give --reference or set {ENV_VAR}")
     out = build(a.reference)
     print(out or "not built")
     sys.exit(0)

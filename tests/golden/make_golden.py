@@ -9,7 +9,8 @@ here (no GPU in the build container):
 Outputs: tests/golden/reference_cpu.npz and tests/golden/reference_meta.json. Inputs are regenerated
 from torch's CPU generator with the recorded seeds, so only outputs (and digests) are stored.
 
-Usage: python tests/golden/make_golden.py [--reference /root/reference]
+Usage: python tests/golden/make_golden.py --reference <reference checkout>
+       (or set G16_REFERENCE_DIR; there is no default location)
 """
 from __future__ import annotations
 
@@ -47,8 +48,11 @@ def sha(t: torch.Tensor) -> str:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("G16_REFERENCE_DIR"),
+                    help="reference checkout (default: $G16_REFERENCE_DIR)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference or set G16_REFERENCE_DIR")
     sys.path.insert(0, os.path.join(a.reference, "src"))
     import gtx16_fp16 as ref  # the reference package
     from gtx16_fp16 import ops as ref_ops

@@ -3,6 +3,7 @@ ShardedMatmul / gather_rows on world_size-2 gloo ranks (the local GEMM is a CPU 
 it is gtx16_fp16.mm_t)."""
 import os
 import socket
+import time
 
 import pytest
 import torch
@@ -75,20 +76,32 @@ def test_sharded_matmul_gloo_world2(n_total):
 
 
 class _FakeMulticast:
-    """Stands in for dist.MulticastBuffer on gloo ranks: construction fails on the ranks listed in
-    `fail`, otherwise it yields a buffer with a multicast address; close() is collective."""
+    """Stands in for dist.MulticastBuffer on gloo ranks. Ranks in `unsupported` report no multicast
+    support; allocation (local) fails on the ranks in `fail`; the rendezvous (collective, like the
+    real one) yields no multicast address on the ranks in `no_mc`. close() is collective, release()
+    local; both are counted."""
+    unsupported = ()
     fail = ()
+    no_mc = ()
     closed = 0
+    released = 0
 
     def __init__(self, shape, dtype, device, group=None):
         if dist.get_rank() in self.fail:
-            raise RuntimeError("multicast object could not be created")
-        self.mc_ptr = 1
+            raise RuntimeError("symmetric memory could not be allocated")
+        self.mc_ptr = 0
         self.group = group
+
+    def rendezvous(self):
+        dist.barrier(group=self.group)
+        self.mc_ptr = 0 if dist.get_rank() in self.no_mc else 1
 
     @staticmethod
     def supported(device):
-        return True
+        return dist.get_rank() not in _FakeMulticast.unsupported
+
+    def release(self):
+        type(self).released += 1
 
     def close(self):
         type(self).closed += 1
@@ -100,12 +113,13 @@ class _FakePeer:
         self.shape = shape
 
 
-def _exchange_worker(rank, world, port, fail, multicast, ret):
+def _exchange_worker(rank, world, port, case, multicast, ret):
     import gtx16_fp16.dist as gdist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        _FakeMulticast.fail = fail
+        for k, v in case.items():
+            setattr(_FakeMulticast, k, v)
         gdist.MulticastBuffer, gdist.PeerBuffer = _FakeMulticast, _FakePeer
         sm = ShardedMatmul(torch.zeros(8, 16), 16 * world, out_dtype=torch.float32,
                            local_mm=lambda x, ws: x @ ws, multicast=multicast)
@@ -115,22 +129,78 @@ def _exchange_worker(rank, world, port, fail, multicast, ret):
         except RuntimeError:
             kind = "raised"
         dist.barrier()  # every rank left the agreement with the same collectives
-        ret[rank] = (kind, _FakeMulticast.closed)
+        ret[rank] = (kind, _FakeMulticast.closed, _FakeMulticast.released)
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fail,multicast,want", [
-    ((), None, {0: ("_FakeMulticast", 0), 1: ("_FakeMulticast", 0)}),
-    ((0,), None, {0: ("_FakePeer", 0), 1: ("_FakePeer", 1)}),
-    ((1,), False, {0: ("_FakePeer", 0), 1: ("_FakePeer", 0)}),
-    ((0,), True, {0: ("raised", 0), 1: ("raised", 1)}),
+MC, PEER = "_FakeMulticast", "_FakePeer"
+
+
+@pytest.mark.parametrize("case,multicast,want", [
+    ({}, None, {0: (MC, 0, 0), 1: (MC, 0, 0)}),
+    # one rank without multicast support: nobody allocates, nobody enters the rendezvous
+    ({"unsupported": (1,)}, None, {0: (PEER, 0, 0), 1: (PEER, 0, 0)}),
+    # one rank's allocation fails: the other releases its copy locally, no rendezvous
+    ({"fail": (0,)}, None, {0: (PEER, 0, 0), 1: (PEER, 0, 1)}),
+    # the rendezvous gives one rank no multicast address: both close (collectively)
+    ({"no_mc": (1,)}, None, {0: (PEER, 1, 0), 1: (PEER, 1, 0)}),
+    ({"fail": (1,)}, False, {0: (PEER, 0, 0), 1: (PEER, 0, 0)}),
+    ({"fail": (0,)}, True, {0: ("raised", 0, 0), 1: ("raised", 0, 1)}),
+    ({"unsupported": (0,)}, True, {0: ("raised", 0, 0), 1: ("raised", 0, 0)}),
 ])
-def test_exchange_buffer_ranks_agree_gloo_world2(fail, multicast, want):
-    """The fused path's buffer choice: one rank's failed multicast set-up sends every rank to peer
-    stores (the rank that built one releases it), multicast=False never tries, multicast=True
-    raises on every rank."""
+def test_exchange_buffer_ranks_agree_gloo_world2(case, multicast, want):
+    """The fused path's buffer choice: whatever one rank finds (no multicast support, a failed
+    allocation, no multicast address) sends every rank to peer stores with the same collectives;
+    multicast=False never tries, multicast=True raises on every rank."""
     world = 2
     ret = mp.Manager().dict()
-    mp.spawn(_exchange_worker, args=(world, _free_port(), fail, multicast, ret), nprocs=world, join=True)
+    mp.spawn(_exchange_worker, args=(world, _free_port(), case, multicast, ret), nprocs=world, join=True)
     assert dict(ret) == want
+
+
+def _leaving_worker(rank, world, port, ret):
+    """Rank 1 takes part in one step of ShardedMatmul and leaves between steps (its process ends,
+    no collective in flight); rank 0 starts the next step and must get an error on the host within
+    the process group's timeout instead of waiting for good."""
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(16, 24, generator=g)
+    w = torch.randn(24, 32, generator=g)
+    n0, n1 = shard_bounds(32, world, rank)
+    sm = ShardedMatmul(w[:, n0:n1].contiguous(), 32, out_dtype=torch.float32, local_mm=lambda x, ws: x @ ws)
+    ok = torch.allclose(sm(a), a @ w, rtol=1e-5, atol=1e-5)  # step 1: both ranks
+    dist.barrier()
+    if rank == 1:
+        ret[rank] = ("left", bool(ok), 0.0)
+        os._exit(0)  # leaves between steps, without any goodbye to its peer
+    time.sleep(0.5)
+    t0 = time.perf_counter()
+    try:
+        sm(a)  # step 2: the peer is gone
+        ret[rank] = ("no error", bool(ok), time.perf_counter() - t0)
+    except RuntimeError:
+        ret[rank] = ("error", bool(ok), time.perf_counter() - t0)
+    os._exit(0)  # the process group cannot be torn down cleanly without the peer
+
+
+def test_rank_leaving_between_steps_is_detected_gloo_world2():
+    world = 2
+    ret = mp.Manager().dict()
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, world, port, ret)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert ret[1][:2] == ("left", True)
+    kind, step1_ok, dt = ret[0]
+    assert step1_ok and kind == "error"
+    assert dt < 30.0  # within the 5 s process-group timeout plus slack, not an endless wait

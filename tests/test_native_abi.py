@@ -79,6 +79,8 @@ def test_argument_checks_return_codes_without_launching():
     assert L.g16_gemm_scatter(p16, p16, dsts, 1, 1, None, None, 16, 8, 8, 8, 0, 5, None) == _native.ERR_ARG
     assert L.g16_ipc_alloc(0, None) == _native.ERR_ARG
     assert L.g16_ipc_open(None, None) == _native.ERR_ARG
+    assert L.g16_selftest_wait_timeout(0, None) == _native.ERR_ARG
+    assert L.g16_selftest_wait_timeout(1000001, None) == _native.ERR_ARG
     assert L.g16_launch_count() == 0
 
 

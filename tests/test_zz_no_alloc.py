@@ -1,10 +1,13 @@
 """g16_gemm_static_scratch, the GEMM entry point for callers that cannot allocate device memory at
-call time (for example a server that reserved all GPU memory for its own pools at start-up). It
-keeps its split-K partial tiles in a fixed 8 MiB array inside libg16 instead of a caller workspace.
+call time (for example a server that reserved all GPU memory for its own pools at start-up). It runs
+g16_gemm's plan, but the one plan that needs scratch memory, the split into fp32 partial tiles,
+keeps them in a fixed 8 MiB array inside libg16 instead of a caller workspace.
 
-Checked through the C ABI against the workspace-based g16_gemm with the same K split, on two calls
+Checked through the C ABI against the workspace-based g16_gemm with the same arguments, on two calls
 in a row (the second on new inputs, so whatever the first call left in the shared array must not
-leak into the result). This file is collected last on purpose."""
+leak into the result). The cases with ksplit > 16 run the partial-tile split, the path that reads
+and writes the array; the others check that the plans needing no scratch are g16_gemm's own. This
+file is collected last on purpose."""
 import pytest
 import torch
 
@@ -33,7 +36,7 @@ def _gemm_static(a, b, bias, out_dtype, ksplit):
     L = _native.lib()
     M, K = a.shape
     N = b.shape[1]
-    out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    out = torch.full((M, N), float("nan"), dtype=out_dtype, device=a.device)
     st = L.g16_gemm_static_scratch(a.data_ptr(), b.data_ptr(), out.data_ptr(), _native.dtype_code(out_dtype),
                                    None if bias is None else bias.data_ptr(), None, M, K, N, ksplit,
                                    _native.stream_handle(a.device.index or 0))
@@ -41,40 +44,57 @@ def _gemm_static(a, b, bias, out_dtype, ksplit):
     return out
 
 
-@pytest.mark.parametrize("M,K,N,ksplit", [(64, 1024, 1024, 4), (128, 16384, 1024, 16), (200, 1032, 136, 3),
-                                          (129, 2048, 264, 8)])
+def _inputs(M, K, N, seed):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(M, K, device="cuda", generator=gen).half()
+    b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
+    bias = torch.randn(N, device="cuda", generator=gen)
+    return a, b, bias
+
+
+@pytest.mark.parametrize("M,K,N,ksplit", [
+    # partial-tile split through the static array (ksplit > 16)
+    (128, 16384, 256, 32),   # 1 tile x 32 chunks = 4 MiB of partials
+    (200, 8192, 256, 20),    # 2 tiles x 20 chunks = 5 MiB
+    (100, 4096, 264, 17),    # 2 tiles, 64 k-blocks: 16 chunks of 4 = 4 MiB, still the partials path
+    (64, 16384, 512, 32),    # 2 tiles x 32 = 8 MiB, the whole array
+    # plans without scratch: in-cluster split, automatic plan (medium-M, small-problem)
+    (64, 1024, 1024, 4), (128, 16384, 1024, 16), (200, 1032, 136, 3), (1024, 4096, 4096, 2),
+    (48, 4096, 768, 0), (2048, 3072, 1024, 0), (128, 16384, 1024, 0),
+])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
 def test_static_scratch_matches_workspace_gemm(cuda_ok, M, K, N, ksplit, out_dtype):
     for call in range(2):  # two calls in a row, new inputs each time
-        gen = torch.Generator(device="cuda").manual_seed(1000 * call + M + K + N)
-        a = torch.randn(M, K, device="cuda", generator=gen).half()
-        b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
-        bias = torch.randn(N, device="cuda", generator=gen)
+        a, b, bias = _inputs(M, K, N, 1000 * call + M + K + N + ksplit)
         ref = _gemm_with_workspace(a, b, bias, out_dtype, ksplit)
         got = _gemm_static(a, b, bias, out_dtype, ksplit)
         torch.cuda.synchronize()
         assert rel_err(got, ref.double()) <= GEMM_NORM
-        assert torch.equal(got, ref)  # same kernel, same K split: identical bits
+        assert torch.equal(got, ref)  # same plan, same K split: identical bits
         assert_close_fp64(got, a, b, bias, out_dtype, f"static scratch call {call}")
 
 
-def test_static_scratch_automatic_split_fits(cuda_ok):
-    # ksplit = 0: the usual split (37 on 148 SMs here) is lowered until 4 tiles x ksplit fit in 8 MiB
-    gen = torch.Generator(device="cuda").manual_seed(7)
-    a = torch.randn(128, 16384, device="cuda", generator=gen).half()
-    b = (torch.randn(16384, 1024, device="cuda", generator=gen) * 16384 ** -0.5).half()
-    for _ in range(2):
-        got = _gemm_static(a, b, None, torch.float16, 0)
-        assert_close_fp64(got, a, b, None, torch.float16, "static scratch, automatic split")
+def test_static_scratch_array_does_not_leak_between_calls(cuda_ok):
+    """A large-split call fills the array; a following call with another shape and split that reads
+    fewer partials gets exactly g16_gemm's result."""
+    a, b, bias = _inputs(64, 16384, 512, 1)
+    _gemm_static(a, b, bias, torch.float32, 32)  # 8 MiB of partials
+    a, b, bias = _inputs(128, 8192, 256, 2)
+    ref = _gemm_with_workspace(a, b, bias, torch.float32, 24)
+    got = _gemm_static(a, b, bias, torch.float32, 24)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
 
 
-def test_static_scratch_rejects_problems_that_do_not_fit(cuda_ok):
-    # 1024 x 4096 output = 128 tiles; two K chunks need 128 x 2 x 128 KiB = 32 MiB > 8 MiB
+def test_static_scratch_rejects_splits_that_do_not_fit(cuda_ok):
+    # 1024 x 4096 output = 128 tiles; 20 K chunks need 128 x 20 x 128 KiB = 320 MiB > 8 MiB
     L = _native.lib()
-    a = torch.empty(1024, 4096, device="cuda", dtype=torch.float16)
-    b = torch.empty(4096, 4096, device="cuda", dtype=torch.float16)
-    out = torch.empty(1024, 4096, device="cuda", dtype=torch.float16)
+    a = torch.zeros(1024, 4096, device="cuda", dtype=torch.float16)
+    b = torch.zeros(4096, 4096, device="cuda", dtype=torch.float16)
+    out = torch.full((1024, 4096), 7.0, device="cuda", dtype=torch.float16)
     st = L.g16_gemm_static_scratch(a.data_ptr(), b.data_ptr(), out.data_ptr(), _native.G16_F16, None, None,
-                                   1024, 4096, 4096, 2, _native.stream_handle(0))
+                                   1024, 4096, 4096, 20, _native.stream_handle(0))
     assert st == _native.ERR_TOO_LARGE
     assert "8 MiB" in _native.strerror(st)
+    torch.cuda.synchronize()
+    assert torch.all(out == 7.0)  # nothing was launched
