@@ -4,13 +4,21 @@
 
 Workloads (a "step" is one call of the hot path on one batch of synthetic input):
   gemm4096   gtx16_fp16.matmul, fp16 4096x4096x4096 -> fp16 (config 3; the headline metric)   [default]
-  skinny     mm_t M=8, K=N=4096, fp32 x, fp16 w_t, fp32 bias/out (config 2)
-  splitk     mm_t 128x16384x1024 fp16 -> fp16 (config 3, split-K shape)
+  gemm1024   gtx16_fp16.matmul, fp16 1024^3 (config 1 on the GPU)
+  skinny*    mm_t M in {1,4,8} at K=N=4096 and M in {1,4} at K=1024, N=3072; fp32 x, fp16 w_t,
+             fp32 bias/out (config 2)
+  splitk*    mm_t 128x16384x1024 and 64x1024x1024 fp16 -> fp16 (config 3, split-K shapes)
   rescale    mm_t 2048x3072x1024 fp32 x with 1% rows x [100,200] (config 4)
+  bert*      BERT-base, 256 x 256 tokens, every Linear patched (config 5); variants with fp16
+             activations and with the GELU/QKV fusion
   decode16   16 FastLinear(4096, 4096) layers at M=1 per step, replayed from a CUDA graph
              (gtx16_fp16.graphs); decode16_eager calls the same layers from Python
-Multi-GPU (--gpus N under torchrun): every listed workload runs as N independent replicas (the path
-has no exchange step for these shapes; scaling "weak"), value = sum over ranks (max-over-ranks time).
+The top-level line is the chosen workload as N independent replicas (no exchange step for these
+shapes; scaling "weak"), value = sum over ranks (max-over-ranks time). `sub` (N=1 only) measures the
+other workloads briefly. `collective` holds the blocks every rank runs at every N: `gemm16384`
+(16384^3 with w_t N-sharded over the ranks and the all-gather fused into the GEMM epilogue; strong
+scaling, fp64 parity on 256 sampled rows, efficiency against the same run's 1-GPU 16384^3) and
+`bert` (data parallel over the 256 sequences, cosine against fp32 over all of them).
 
 Timing: W untimed warm-up steps, then K steps between barrier + synchronize, timed with CUDA events
 on the launching stream. Inputs rotate over several sets whose total exceeds the 126 MB L2, so every
@@ -18,6 +26,8 @@ step reads its operands from HBM. Clocks and throttle reasons are sampled with N
 region. `e2e` repeats the step through the public API from pinned host memory (H2D of the inputs and
 D2H of the result inside the timed region). `cpu_baseline` times the reference's CPU path
 (oracle/cpu_path.py: torch fp32 matmul) on a bounded sample on the host cores (rank 0, N=1 only).
+Each roofline is the binding one of its shape: FLOPs at the measured bf16 peak or algorithmic bytes
+at the measured copy bandwidth, whichever takes longer.
 """
 from __future__ import annotations
 
@@ -165,14 +175,22 @@ def _rotating_sets(nbytes_per_set: int) -> int:
     return max(3, int(2 * L2_BYTES // max(nbytes_per_set, 1)) + 1)
 
 
+def binding_bound(flops: float, nbytes: float, peaks: dict) -> str:
+    """"tensor" or "hbm": whichever roofline takes longer for this much work (FLOPs at the measured
+    bf16 peak against algorithmic bytes at the measured copy bandwidth)."""
+    t_tensor = flops / (peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]) * 1e12)
+    t_hbm = nbytes / (peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]) * 1e9)
+    return "tensor" if t_tensor >= t_hbm else "hbm"
+
+
 class Gemm(Workload):
     """gtx16_fp16.matmul: fp16 A[M,K] @ fp16 B[K,N] -> fp16."""
-    bound = "tensor"
 
     def __init__(self, dev, M, K, N, name):
         super().__init__(dev)
         self.M, self.K, self.N = M, K, N
         self.name = name
+        self.bound = binding_bound(self.flops(), self.alg_bytes(), load_peaks()[0])
         self.metric = f"GEMM TFLOPS (fp16 {M}x{K}x{N}, gtx16_fp16.matmul)"
         self.unit = "TFLOPS"
         per = (M * K + K * N + M * N) * 2
@@ -230,7 +248,7 @@ class MmT(Workload):
         self.name = name
         self.xdt, self.out_dtype = xdt, out_dtype
         self.skinny = M <= 8
-        self.bound = "hbm" if self.skinny else "tensor"
+        self.bound = "hbm" if self.skinny else binding_bound(self.flops(), self.alg_bytes(), load_peaks()[0])
         self.metric = (f"skinny mm_t HBM GB/s (M={M}, {K}x{N})" if self.skinny else
                        f"mm_t TFLOPS ({M}x{K}x{N}{', overflow rescale' if rescale else ''})")
         self.unit = "GB/s" if self.skinny else "TFLOPS"
@@ -304,7 +322,7 @@ class ShardedGemm(Workload):
     graphable = False
     multicast = None  # ShardedMatmul.multicast: None = NVLink multicast where supported, False = peer stores
 
-    def __init__(self, dev, world, rank, M=16384, K=16384, N=16384):
+    def __init__(self, dev, world, rank, M=16384, K=16384, N=16384, sample_rows=0, keep_full_b=False):
         super().__init__(dev)
         from gtx16_fp16.dist import ShardedMatmul, shard_bounds
         self.M, self.K, self.N, self.world, self.rank = M, K, N, world, rank
@@ -317,15 +335,43 @@ class ShardedGemm(Workload):
         self.A = torch.randn(M, K, device=dev, generator=g).half()
         n0, n1 = shard_bounds(N, world, rank)
         b = torch.empty(K, n1 - n0, device=dev, dtype=torch.float16)
+        self.B_full = torch.empty(K, N, device=dev, dtype=torch.float16) if keep_full_b else None
+        # fp64 truth for `sample_rows` seeded rows of the full output: A[rows] @ B, panel by panel
+        self.rows = None
+        if sample_rows:
+            self.rows = torch.randperm(M, generator=torch.Generator().manual_seed(1))[:sample_rows].sort().values
+            a_s = self.A[self.rows.to(dev)].double()
+            self.ref_rows = torch.empty(sample_rows, N, device=dev, dtype=torch.float64)
+            self.mag_rows = torch.empty(sample_rows, N, device=dev, dtype=torch.float64)
         # B ~ N(0, 1/sqrt(K)) generated in 2048-column panels so every rank draws the same B
         for c0 in range(0, N, 2048):
             panel = (torch.randn(K, min(2048, N - c0), device=dev, generator=g) * K ** -0.5).half()
-            lo, hi = max(c0, n0), min(c0 + panel.shape[1], n1)
+            c1 = c0 + panel.shape[1]
+            lo, hi = max(c0, n0), min(c1, n1)
             if lo < hi:
                 b[:, lo - n0:hi - n0] = panel[:, lo - c0:hi - c0]
+            if self.B_full is not None:
+                self.B_full[:, c0:c1] = panel
+            if sample_rows:
+                p64 = panel.double()
+                self.ref_rows[:, c0:c1] = a_s @ p64
+                self.mag_rows[:, c0:c1] = a_s.abs() @ p64.abs()
+                del p64
             del panel
+        if sample_rows:
+            del a_s
         self.B = b
         self.sm = ShardedMatmul(self.B, N, out_dtype=torch.float16, multicast=self.multicast)
+
+    def check_rows(self, out):
+        """(norm-wise, component-wise) relative error of the sampled rows of the full output against
+        fp64: ||y - ref|| / ||ref|| and max |y - ref| / (|A| @ |B|)."""
+        y = out[self.rows.to(out.device)].double()
+        d = y - self.ref_rows
+        norm = float(d.norm() / self.ref_rows.norm())
+        comp = float((d.abs() / self.mag_rows.clamp_min(1e-300)).max())
+        finite = bool(torch.isfinite(y).all())
+        return norm, comp, finite
 
     def config(self):
         return {"workload": self.name, "M": self.M, "K": self.K, "N": self.N, "in": "fp16", "out": "fp16",
@@ -563,6 +609,7 @@ WORKLOADS = {
     "skinny1": lambda dev, w, r: MmT(dev, 1, 4096, 4096, "skinny1", torch.float32, torch.float32, 0.02, 0.01),
     "skinny4": lambda dev, w, r: MmT(dev, 4, 4096, 4096, "skinny4", torch.float32, torch.float32, 0.02, 0.01),
     "skinny1x3072": lambda dev, w, r: MmT(dev, 1, 1024, 3072, "skinny1x3072", torch.float32, torch.float32, 0.02, 0.01),
+    "skinny4x3072": lambda dev, w, r: MmT(dev, 4, 1024, 3072, "skinny4x3072", torch.float32, torch.float32, 0.02, 0.01),
     "rescale": lambda dev, w, r: MmT(dev, 2048, 3072, 1024, "rescale", torch.float32, torch.float32, 0.02, 0.0,
                                      rescale=True),
     "bert": lambda dev, w, r: Bert(dev, w, r),
@@ -717,8 +764,13 @@ def run_ours(args, rank, world, dev):
             "timing": "CUDA graph of the K steps, replayed once" if graph is not None else "eager launches"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl)
-    if rank == 0 and args.extra:
+    del wl
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and args.extra:
         line["sub"] = sub_metrics(args, dev, g16, peaks)
+    if args.blocks:
+        line["collective"] = {name: BLOCKS[name](args, rank, world, dev, peaks)
+                              for name in args.blocks.split(",") if name}
     return line
 
 
@@ -781,21 +833,137 @@ def sub_metrics(args, dev, g16, peaks):
             with torch.cuda.stream(stream):
                 graph.replay()
             torch.cuda.synchronize(dev)
+        cos = wl.check_cosine() if isinstance(wl, Bert) else None
         ms = timed_loop(wl, g16, steps, stream, graph) / steps
         if wl.unit == "texts/s":
             v = wl.batch / (ms * 1e-3)
-            frac = wl.flops() / (ms * 1e-3) / 1e12 / peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
         elif wl.unit == "TFLOPS":
             v = wl.flops() / (ms * 1e-3) / 1e12
-            frac = v / peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
         else:
             v = wl.alg_bytes() / (ms * 1e-3) / 1e9
-            frac = v / peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+        if wl.bound == "tensor":
+            frac = wl.flops() / (ms * 1e-3) / 1e12 / peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        else:
+            frac = wl.alg_bytes() / (ms * 1e-3) / 1e9 / peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
         out[name] = {"value": round(v, 2), "unit": wl.unit, "us_per_step": round(ms * 1e3, 2),
-                     "frac_of_measured_peak": round(frac, 4), "config": wl.config()}
+                     "bound": wl.bound, "frac_of_measured_peak": round(frac, 4),
+                     "basis": ("2*M*N*K FLOP at the bf16 burst peak" if wl.bound == "tensor" else
+                               "algorithmic bytes at the measured copy bandwidth"),
+                     "config": wl.config()}
+        if cos is not None:
+            out[name]["cosine_min_vs_fp32"] = cos
         del wl
         torch.cuda.empty_cache()
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# Collective blocks: every rank takes part, at every N (the strong-scaling evidence of the line)
+# ---------------------------------------------------------------------------------------------
+def timed_eager(fn, steps, world, dev):
+    """Max-over-ranks device milliseconds per step of `fn` (CUDA events, barrier + sync around)."""
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    barrier(world)
+    return reduce_max(start.elapsed_time(end), world, dev) / steps
+
+
+def block_gemm16384(args, rank, world, dev, peaks):
+    """16384^3 fp16 GEMM, w_t N-sharded over all ranks with the all-gather fused into the GEMM
+    epilogue (gtx16_fp16.dist.ShardedMatmul); TFLOPS of the whole job, max-over-ranks time.
+    Parity: 256 seeded rows of the full gathered output on every rank against fp64 (norm-wise and
+    component-wise, worst rank). Efficiency: against the same run's 1-GPU 16384^3 (the full
+    unsharded GEMM through gtx16_fp16.matmul on each rank's GPU; the fastest GPU is the baseline)."""
+    import gtx16_fp16 as g16
+    from gtx16_fp16 import _native
+    wl = ShardedGemm(dev, world, rank, sample_rows=256, keep_full_b=world > 1)
+    steps = args.block_steps
+    for _ in range(3):
+        wl.step(g16)
+    l0 = _native.launch_count()
+    ms = timed_eager(lambda: wl.step(g16), steps, world, dev)
+    launches = (_native.launch_count() - l0) / steps
+    flops = 2.0 * wl.M * wl.N * wl.K
+    tflops = flops / (ms * 1e-3) / 1e12
+    out = wl.step(g16)
+    torch.cuda.synchronize(dev)
+    norm, comp, finite = wl.check_rows(out)
+    norm, comp = reduce_max(norm, world, dev), reduce_max(comp, world, dev)
+    finite = reduce_max(0.0 if finite else 1.0, world, dev) == 0.0
+    exchange = wl.exchange()
+    wl.close()
+    if world > 1:
+        a, b = wl.A, wl.B_full
+        for _ in range(3):
+            g16.matmul(a, b)
+        torch.cuda.synchronize(dev)
+        stream = torch.cuda.current_stream(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(steps):
+            g16.matmul(a, b)
+        e.record(stream)
+        e.synchronize()
+        one_ms = -reduce_max(-s.elapsed_time(e) / steps, world, dev)  # fastest GPU
+        barrier(world)
+    else:
+        one_ms = ms
+    one_tflops = flops / (one_ms * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    res = {"value": round(tflops, 2), "unit": "TFLOPS", "ms_per_step": round(ms, 4), "steps": steps,
+           "n_gpus": world, "scaling": "strong", "exchange": exchange,
+           "one_gpu_tflops": round(one_tflops, 2),
+           "efficiency_vs_1gpu": round(tflops / (world * one_tflops), 4),
+           "per_gpu_frac_of_measured_peak": round(tflops / world / peak, 4),
+           "parity": {"rows": int(wl.rows.numel()), "norm_rel_err_vs_fp64": norm,
+                      "componentwise_rel_err_vs_fp64": comp, "finite": finite,
+                      "tolerance": 1e-3, "pass": bool(finite and norm <= 1e-3 and comp <= 1e-3),
+                      "checked_on": "every rank (worst rank reported)"},
+           "gpu_launches_per_step": launches,
+           "config": dict(wl.config(), parallelism=f"n-shard{world}",
+                          timing="eager steps, CUDA events, max over ranks",
+                          one_gpu_baseline="gtx16_fp16.matmul 16384^3 on each GPU of this run, fastest GPU")}
+    del wl
+    torch.cuda.empty_cache()
+    return res
+
+
+def block_bert(args, rank, world, dev, peaks):
+    """BERT-base (config 5), data parallel over the 256 sequences; texts/s = 256 / max-rank step
+    time. Cosine of the CLS embeddings against the unpatched fp32 model on every rank's slice, so
+    all 256 sequences are checked; the worst one is reported."""
+    import gtx16_fp16 as g16
+    from gtx16_fp16 import _native
+    wl = Bert(dev, world, rank)
+    cos = -reduce_max(-wl.check_cosine(), world, dev)
+    for _ in range(3):
+        wl.step(g16)
+    l0 = _native.launch_count()
+    ms = timed_eager(lambda: wl.step(g16), args.bert_steps, world, dev)
+    launches = (_native.launch_count() - l0) / args.bert_steps
+    linear_tflops = world * wl.flops() / (ms * 1e-3) / 1e12  # approximate: slices differ by <= 1 sequence
+    res = {"value": round(wl.batch / (ms * 1e-3), 2), "unit": "texts/s", "ms_per_step": round(ms, 3),
+           "steps": args.bert_steps, "n_gpus": world, "scaling": "strong",
+           "cosine_min_vs_fp32": round(cos, 7), "cosine_target": 0.9999, "sequences_checked": wl.batch,
+           "linear_tflops": round(linear_tflops, 2),
+           "linear_frac_of_measured_peak": round(linear_tflops / world /
+                                                 peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]), 4),
+           "gpu_launches_per_step": launches,
+           "config": dict(wl.config(), parallelism=f"dp{world}", cosine_min_vs_fp32=round(cos, 7),
+                          timing="eager steps, CUDA events, max over ranks")}
+    del wl
+    torch.cuda.empty_cache()
+    return res
+
+
+BLOCKS = {"gemm16384": block_gemm16384, "bert": block_bert}
 
 
 def cpu_baseline(wl):
@@ -871,8 +1039,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="gemm4096", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--extra", default="skinny1,skinny4,skinny,splitk,splitk64,rescale,decode16,decode16_eager",
-                    help="comma list of other workloads measured briefly into 'sub' (rank 0); '' to skip")
+    ap.add_argument("--extra", default=("gemm1024,skinny1,skinny4,skinny,skinny1x3072,skinny4x3072,splitk,splitk64,"
+                                        "rescale,decode16,decode16_eager,bert_fused,bert16"),
+                    help="comma list of other workloads measured briefly into 'sub' (N=1 only); '' to skip")
+    ap.add_argument("--blocks", default="gemm16384,bert",
+                    help="comma list of collective blocks every rank runs at every N ('collective'); '' to skip")
+    ap.add_argument("--block-steps", type=int, default=10, help="timed steps of the gemm16384 block")
+    ap.add_argument("--bert-steps", type=int, default=5, help="timed steps of the bert block")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graph", type=int, default=1, help="1: time a CUDA graph of the K steps (default); 0: eager")
     ap.add_argument("--exchange", default="auto", choices=["auto", "peer"],

@@ -33,6 +33,63 @@ def test_bert_base_patched_cosine(cuda_ok):
     assert cos.min().item() >= 0.9999, cos.min().item()
 
 
+def test_bert_base_patched_cosine_full_batch(cuda_ok):
+    """BASELINE config 5 at its full size: 256 sequences x 256 tokens through the patched model
+    (73 FastLinear layers, fp32 activations), CLS cosine >= 0.9999 against the unpatched fp32 model
+    for every one of the 256 sequences."""
+    transformers = pytest.importorskip("transformers")
+    cfg = transformers.BertConfig(vocab_size=30522, hidden_size=768, num_hidden_layers=12, num_attention_heads=12,
+                                  intermediate_size=3072, hidden_act="gelu", max_position_embeddings=512,
+                                  attn_implementation="sdpa")
+    torch.manual_seed(0)
+    model = transformers.BertModel(cfg).eval()
+    ref_model = copy.deepcopy(model).cuda()
+    model = model.cuda()
+    assert g.patch(model, force=True) == 73
+    gen = torch.Generator().manual_seed(0)
+    ids = torch.randint(1000, 30522, (256, 256), generator=gen).cuda()
+    mask = torch.ones_like(ids)
+    with torch.no_grad():
+        ref = ref_model(input_ids=ids, attention_mask=mask).last_hidden_state[:, 0]
+        got = model(input_ids=ids, attention_mask=mask).last_hidden_state[:, 0]
+    assert torch.isfinite(got).all()
+    cos = (torch.nn.functional.normalize(ref.float(), dim=-1) * torch.nn.functional.normalize(got.float(), dim=-1)).sum(-1)
+    assert cos.numel() == 256
+    assert cos.min().item() >= 0.9999, cos.min().item()
+
+
+def test_gemm_16384_cubed_sampled_rows_vs_fp64(cuda_ok):
+    """BASELINE config 3's 16384^3 on one GPU (the single-pass CTA-pair kernel), A ~ N(0,1),
+    B ~ N(0, 1/sqrt(K)), fp16 out: 256 seeded rows of the output against fp64, norm-wise and
+    component-wise within 1e-3, no inf/NaN anywhere in the 16384 x 16384 output."""
+    from _tol import GEMM_NORM, GEMM_RTOL
+    M = K = N = 16384
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(M, K, device="cuda", generator=gen).half()
+    b = (torch.randn(K, N, device="cuda", generator=gen) * K ** -0.5).half()
+    y = g.matmul(a, b)
+    assert y.dtype == torch.float16 and y.shape == (M, N)
+    assert torch.isfinite(y).all()
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(1))[:256].sort().values.cuda()
+    a_s = a[rows].double()
+    ys = y[rows].double()
+    d2 = r2 = 0.0
+    comp = 0.0
+    for c0 in range(0, N, 2048):
+        p = b[:, c0:c0 + 2048].double()
+        ref = a_s @ p
+        mag = a_s.abs() @ p.abs()
+        d = ys[:, c0:c0 + 2048] - ref
+        d2 += float((d * d).sum())
+        r2 += float((ref * ref).sum())
+        comp = max(comp, float((d.abs() / mag).max()))
+    norm = (d2 / r2) ** 0.5
+    assert norm <= GEMM_NORM, norm
+    assert comp <= GEMM_RTOL, comp
+    # bitwise reproducible at this size too
+    assert torch.equal(g.matmul(a, b)[rows], y[rows])
+
+
 def test_bert_base_fp16_activations_mode(cuda_ok):
     """patch(..., activations=torch.float16): the whole model runs with fp16 activations (opt-in;
     the reference's FastLinear keeps fp32 activations). FastLinear keeps weight_t fp16 and bias

@@ -11,7 +11,7 @@ import torch.nn.functional as F
 import gtx16_fp16 as g
 from gtx16_fp16 import _native
 
-from _tol import GEMM_NORM, assert_close_fp64, ref64, rel_err
+from _tol import GEMM_NORM, assert_close_fp64, bounds, ref64, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -162,9 +162,12 @@ def test_large_outputs_do_not_overflow_with_fp32_out(cuda_ok):
     assert torch.all(y == 16 * 16 * 4096)  # exact in fp32 accumulation
 
 
-@pytest.mark.parametrize("M", [1, 5, 64, 300])
+@pytest.mark.parametrize("M", [1, 5, 8, 9, 64, 300])
 @pytest.mark.parametrize("in_dtype", [torch.float32, torch.float16])
 def test_massive_activations_do_not_overflow(cuda_ok, M, in_dtype):
+    """The reference's massive-activation case (tests/test_correctness.py:112-126): a column at
+    179,940 and one element at -120,000. The skinny path (M <= 8, fp32 out) is held to its own
+    1e-5 bound against fp64, the GEMM path to 1e-3 (both norm-wise and component-wise)."""
     torch.manual_seed(1)
     K, N = 3072, 1024
     x = torch.randn(M, K, device="cuda")
@@ -175,7 +178,9 @@ def test_massive_activations_do_not_overflow(cuda_ok, M, in_dtype):
     y = g.mm_t(x, w, None, torch.float32)
     assert torch.isfinite(y).all()
     assert rel_err(y, x.float() @ w.float()) < 2e-3
-    assert rel_err(y, ref64(x, w)) < GEMM_NORM
+    norm, rtol = bounds(M, torch.float32)
+    assert rel_err(y, ref64(x, w)) < norm
+    assert_close_fp64(y, x, w, None, torch.float32, f"massive activations M={M}")
 
 
 def test_is_affected_reports_bool(cuda_ok):
