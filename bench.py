@@ -399,8 +399,10 @@ class ShardedGemm(Workload):
         bufs = list(self.sm._bufs.values())
         if not bufs:
             return "not run"
-        return ("NVLink multicast stores (multimem.st) from the GEMM epilogue"
-                if isinstance(bufs[0], MulticastBuffer) else "peer TMA stores from the GEMM epilogue (CUDA IPC)")
+        return ("NVLink multicast stores (multimem.st) from the GEMM epilogue; completion signalled by the "
+                "kernel through a multicast counter, no host collective per call"
+                if isinstance(bufs[0], MulticastBuffer) else
+                "peer TMA stores from the GEMM epilogue (CUDA IPC); two NCCL all-reduces per call order buffer reuse")
 
     def close(self):
         self._exchange = self.exchange()

@@ -57,6 +57,10 @@ struct PairDst {
   // 128-byte row segment is written once with multimem.st and reaches every GPU's copy.
   uint64_t mc;
   long long ldc;
+  // Multicast mode only, optional (0: none): a 32-bit counter behind an NVLink multicast address.
+  // Each CTA adds 1 to it on every GPU once all its stores are issued and fenced, so a GPU whose
+  // counter has grown by (CTAs per rank x ranks) holds every rank's tiles.
+  uint64_t mc_flag;
 };
 
 struct PairArgs {
@@ -331,10 +335,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   }
 
   // Every tile store has completed (and, for peer destinations, is visible system-wide) before the
-  // grid ends.
-  if (warp >= 2 && lane == 0) {
-    bulk_wait_group0();
-    if (dst.ndst != 1) __threadfence_system();
+  // grid ends. In multicast mode every lane stored, so every lane fences.
+  if (warp >= 2) {
+    if (lane == 0) bulk_wait_group0();
+    if (dst.ndst == 0 || (dst.ndst > 1 && lane == 0)) __threadfence_system();
   }
   // TMEM is released only after every MMA of the pair has completed and both CTAs are done.
   if (warp == 1) {
@@ -344,6 +348,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
+  // Completion signal (multicast mode): the cluster barrier above orders every thread's fenced
+  // stores before this release, which reaches every GPU's counter through the switch.
+  if (threadIdx.x == 0 && dst.mc_flag != 0) {
+    __threadfence_system();
+    multimem_red_add_release_u32(dst.mc_flag, 1u);
+  }
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc_pair(tmem, kPrTmemCols);
@@ -468,7 +478,7 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
 
 int launch_gemm_pair_multimem(const uint16_t* a16, const uint16_t* b16, void* mc, int out_dtype, const float* bias,
                               const float* rscale, int M, int K, int N, long long ldc, int col0, cudaStream_t s,
-                              const DeviceInfo& dev) {
+                              const DeviceInfo& dev, void* mc_flag) {
   if (mc == nullptr) return G16_ERR_ARG;
   if (M <= 0 || N <= 0) return G16_OK;
   PairDst dmaps{};
@@ -476,7 +486,15 @@ int launch_gemm_pair_multimem(const uint16_t* a16, const uint16_t* b16, void* mc
   dmaps.col0 = col0;
   dmaps.mc = reinterpret_cast<uint64_t>(mc);
   dmaps.ldc = ldc;
+  dmaps.mc_flag = reinterpret_cast<uint64_t>(mc_flag);
   return launch_pair_impl(a16, b16, dmaps, out_dtype, bias, rscale, M, K, N, s, dev, G16_ACT_NONE);
+}
+
+int gemm_pair_ctas(int M, int N, const DeviceInfo& dev) {
+  if (M <= 0 || N <= 0) return 0;
+  const int units = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
+  const int max_pairs = dev.sm_count / 2;
+  return 2 * (units < max_pairs ? units : max_pairs);
 }
 
 int launch_gemm_pair_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,

@@ -63,9 +63,12 @@ bool gemm_pair_available();
 // stores; peer buffers for the multi-GPU exchange).
 // The same with every tile written once through an NVLink multicast address covering all ranks'
 // [M, ldc] outputs (multimem.st; the switch replicates it).
+// mc_flag (optional): multicast address of a 32-bit counter every CTA adds 1 to after its stores.
 int launch_gemm_pair_multimem(const uint16_t* a16, const uint16_t* b16, void* mc, int out_dtype, const float* bias,
                               const float* rscale, int M, int K, int N, long long ldc, int col0, cudaStream_t s,
-                              const DeviceInfo& dev);
+                              const DeviceInfo& dev, void* mc_flag = nullptr);
+// CTAs the pair kernel launches for an [M, N] output (each signals once in multicast mode).
+int gemm_pair_ctas(int M, int N, const DeviceInfo& dev);
 int launch_gemm_pair_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
                              const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
                              cudaStream_t s, const DeviceInfo& dev);

@@ -427,6 +427,19 @@ __device__ __forceinline__ void multimem_st_v4(uint64_t mc_addr, uint4 v) {
                : "memory");
 }
 
+// Adds v to a 32-bit counter on every GPU bound to an NVLink multicast address, with release
+// semantics at system scope: whatever this thread's CTA wrote before (ordered by a barrier and a
+// system fence) is visible to a reader that acquires the new value.
+__device__ __forceinline__ void multimem_red_add_release_u32(uint64_t mc_addr, uint32_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc_addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Streaming 128-bit global load that does not allocate in L1 (weights are read exactly once).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;

@@ -41,6 +41,9 @@ SIGNATURES = {
     "g16_gemm_static_scratch": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P]),
     "g16_gemm_scatter": (_I, [_P, _P, ctypes.POINTER(_P), _I, _I, _P, _P, _I, _I, _I, ctypes.c_longlong, _I, _I,
                               _P]),
+    "g16_gemm_allgather_mc": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, ctypes.c_longlong, _I, _P, _P,
+                                   ctypes.c_uint32, _I, _P]),
+    "g16_gemm_allgather_signals": (_I, [_I, _I, _I]),
     "g16_ipc_alloc": (_I, [_Z, ctypes.POINTER(_P)]),
     "g16_ipc_free": (_I, [_P]),
     "g16_ipc_get_handle": (_I, [_P, _P]),

@@ -8,11 +8,17 @@ shapes that shard naturally:
   fp16 activations the exchange is fused into the GEMM: where the GPUs support NVLink multicast
   (NVLS) the epilogue writes every output tile once through a multicast address bound to all
   ranks' output buffers (``MulticastBuffer``: torch symmetric memory) and the switch delivers it
-  everywhere; otherwise it stores every tile into each rank's full output buffer (``PeerBuffer``:
-  CUDA IPC mappings over NVLink). Either way the all-gather overlaps the math and no separate
-  copy pass is needed; two one-element all-reduces per call order the buffers' reuse. Otherwise (fp32 activations, M <= 8, gloo) the shards are
-  computed with ``mm_t`` and exchanged with one NCCL all-gather. Every rank ends with the full
-  output. Shard boundaries are multiples of 8 columns (the kernels' N % 8 rule).
+  everywhere; the kernel's CTAs then signal a multicast counter and a bounded wait on this GPU's
+  copy of it ends the call (g16_gemm_allgather_mc), so a call makes no host collective at all. Two
+  output slots alternate: a peer writes the slot of call i + 1 only after this rank's kernel of
+  call i has finished, i.e. after this rank's stream has passed everything it enqueued before
+  call i, including its reads of the result of call i - 1 (the same slot).
+  Without multicast the epilogue stores every tile into each rank's full output buffer
+  (``PeerBuffer``: CUDA IPC mappings over NVLink) and two one-element all-reduces per call order
+  the buffer's reuse. Either way the all-gather overlaps the math and no separate copy pass is
+  needed. Otherwise (fp32 activations, M <= 8, gloo) the shards are computed with ``mm_t`` and
+  exchanged with one NCCL all-gather. Every rank ends with the full output. Shard boundaries are
+  multiples of 8 columns (the kernels' N % 8 rule).
 * ``batch_slice``: data parallelism over a batch of independent inputs (model inference): rank r
   takes a contiguous slice; there is no collective on the data path, only an optional gather of
   the (small) results.
@@ -212,16 +218,18 @@ class ShardedMatmul:
         if buf is None:
             buf = self._exchange_buffer(M, a.device)
             self._bufs[M] = buf
-            self._flag = torch.zeros(1, dtype=torch.int32, device=a.device)
+            if isinstance(buf, MulticastBuffer):
+                self._init_signals(buf, M, K, a.device)
+            else:
+                self._flag = torch.zeros(1, dtype=torch.int32, device=a.device)
+        if isinstance(buf, MulticastBuffer):
+            return self._multicast_call(buf, a, out)
         # Peers are done with their outputs of the previous call before any tile lands there.
         dist.all_reduce(self._flag, group=self.group)
-        if isinstance(buf, MulticastBuffer):
-            ptrs, ndst, flags = (ctypes.c_void_p * 1)(buf.mc_ptr), 1, _native.SCATTER_MULTIMEM
-        else:
-            ptrs, ndst, flags = (ctypes.c_void_p * self.world)(*buf.ptrs), self.world, self.scatter_flags
+        ptrs = (ctypes.c_void_p * self.world)(*buf.ptrs)
         st = _native.lib().g16_gemm_scatter(
-            a.data_ptr(), self.w_shard.data_ptr(), ptrs, ndst, _native.dtype_code(self.out_dtype), None,
-            None, M, K, self.n1 - self.n0, self.n_total, self.n0, flags,
+            a.data_ptr(), self.w_shard.data_ptr(), ptrs, self.world, _native.dtype_code(self.out_dtype), None,
+            None, M, K, self.n1 - self.n0, self.n_total, self.n0, self.scatter_flags,
             _native.stream_handle(a.device.index or 0))
         _native.check(st, "g16_gemm_scatter")
         # Every peer's kernel (and so every tile it stored here) has completed.
@@ -230,6 +238,44 @@ class ShardedMatmul:
             out.copy_(buf.tensor)
             return out
         return buf.tensor
+
+    # Longest a rank's stream waits for its peers' tiles before the library records a timeout.
+    SIGNAL_WAIT_US = 30_000_000
+
+    def _init_signals(self, buf: MulticastBuffer, M: int, K: int, device: torch.device):
+        """Set-up of the multicast path (collective): zero every GPU's counter before any rank can
+        signal, and agree on the counter increments per call (the CTAs of all ranks)."""
+        from . import _native
+        n = _native.lib().g16_gemm_allgather_signals(M, K, self.n1 - self.n0)
+        if n < 0:
+            raise _native.G16Error(-n, "g16_gemm_allgather_signals")
+        total = torch.tensor([n], dtype=torch.int64, device=device)
+        dist.all_reduce(total, group=self.group)
+        buf.flag.tensor.zero_()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)  # every counter is zero before the first signal
+        buf.signals = int(total.item())
+        buf.target = 0
+        buf.calls = 0
+
+    def _multicast_call(self, buf: MulticastBuffer, a: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+        from . import _native
+        M, K = a.shape
+        slot = buf.calls % 2
+        buf.calls += 1
+        buf.target = (buf.target + buf.signals) & 0xFFFFFFFF
+        esz = torch.tensor([], dtype=self.out_dtype).element_size()
+        st = _native.lib().g16_gemm_allgather_mc(
+            a.data_ptr(), self.w_shard.data_ptr(), buf.mc_ptr + slot * M * self.n_total * esz,
+            _native.dtype_code(self.out_dtype), None, None, M, K, self.n1 - self.n0, self.n_total, self.n0,
+            buf.flag.mc_ptr, buf.flag.tensor.data_ptr(), buf.target, self.SIGNAL_WAIT_US,
+            _native.stream_handle(a.device.index or 0))
+        _native.check(st, "g16_gemm_allgather_mc")
+        res = buf.tensor[slot * M:(slot + 1) * M]
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
 
     def _exchange_buffer(self, M: int, device: torch.device):
         """The output buffer of the fused path for M rows (collective). A MulticastBuffer where every
@@ -247,31 +293,42 @@ class ShardedMatmul:
             return bool(t.item())
 
         if self.multicast is not False and agree(MulticastBuffer.supported(device)):
+            # two output slots, used alternately, and the completion counter (multicast too)
+            bufs = []
             try:
-                buf = MulticastBuffer((M, self.n_total), self.out_dtype, device, self.group)
+                bufs.append(MulticastBuffer((2 * M, self.n_total), self.out_dtype, device, self.group))
+                bufs.append(MulticastBuffer((1, 64), torch.int32, device, self.group))
             except RuntimeError:
-                buf = None
-            if agree(buf is not None):
-                buf.rendezvous()
-                if agree(buf.mc_ptr != 0):
-                    return buf
-                buf.close()
-            elif buf is not None:
-                buf.release()
+                pass
+            if agree(len(bufs) == 2):
+                for b in bufs:
+                    b.rendezvous()
+                if agree(all(b.mc_ptr != 0 for b in bufs)):
+                    bufs[0].flag = bufs[1]
+                    return bufs[0]
+                for b in bufs:
+                    b.close()
+            else:
+                for b in bufs:
+                    b.release()
         if self.multicast:
             raise RuntimeError("ShardedMatmul(multicast=True): no NVLink multicast on this group")
         return PeerBuffer((M, self.n_total), self.out_dtype, device, self.group)
 
     def close(self):
-        """Release the fused path's peer buffers (collective: every rank calls it)."""
+        """Release the fused path's buffers (collective: every rank calls it)."""
         for buf in self._bufs.values():
+            flag = getattr(buf, "flag", None)
             buf.close()
+            if flag is not None:
+                flag.close()
         self._bufs.clear()
 
     def __call__(self, a: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """The full [M, N] output on every rank. On the fused path the returned tensor is this
-        instance's output buffer for M rows: it stays valid until the next call with the same M
-        (or ``close()``); pass ``out`` to keep a copy."""
+        """The full [M, N] output on every rank. On the fused path the returned tensor is one of
+        this instance's output buffers for M rows: it stays valid until this rank's next call with
+        the same M (or ``close()``), and must be read on the calling stream; pass ``out`` to keep a
+        copy."""
         if self.fused_applies(a):
             return self._fused_call(a, out)
         c_local = self.local(a).contiguous()

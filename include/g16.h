@@ -173,6 +173,32 @@ int g16_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst,
                      int flags, void* stream);
 
 /*
+ * No counterpart in the reference (it has no multi-GPU path): the column-sharded GEMM with both the
+ * output all-gather and the completion barrier fused into the kernel, so a call needs no host
+ * collective. mc_out: NVLink multicast address bound to every rank's [M, ldc] output buffer (as for
+ * G16_SCATTER_MULTIMEM); this rank's tiles land at column col0 of every copy. mc_flag: multicast
+ * address of a 32-bit counter bound on every rank; flag: this GPU's copy of it. After its last
+ * store each CTA of every rank adds 1 to the counter on every GPU (multimem.red.release.sys); a
+ * one-thread kernel, enqueued after the GEMM, then waits until this GPU's counter reaches `target`
+ * (compared mod 2^32), so later work on `stream` sees every rank's tiles. The caller keeps the
+ * running target: previous target + the sum over all ranks of g16_gemm_allgather_signals(M, K, N)
+ * (counters start at 0 on every GPU before the first call). The wait is bounded by wait_limit_us
+ * (1 .. 60,000,000): on expiry it records G16_ERR_TIMEOUT in the device status word
+ * (g16_device_status) and returns. Consecutive calls must use different output buffers (a peer may
+ * start call i + 1 while this rank still reads the result of call i); alternating two buffers is
+ * enough when each rank reads a result on `stream` before its next call, because a peer's call
+ * i + 1 starts only after this rank's kernel of call i, and so its reads of the result of call
+ * i - 1 enqueued before it, has finished. Requirements as g16_gemm_scatter;
+ * G16_ERR_UNSUPPORTED where a CTA-pair cluster cannot be resident.
+ */
+int g16_gemm_allgather_mc(const uint16_t* a16, const uint16_t* b16, void* mc_out, int out_dtype, const float* bias,
+                          const float* rscale, int M, int K, int N, long long ldc, int col0, void* mc_flag,
+                          const uint32_t* flag, uint32_t target, int wait_limit_us, void* stream);
+/* Counter increments one g16_gemm_allgather_mc call of this rank makes on every GPU (its CTAs), or
+ * minus a g16_status code. */
+int g16_gemm_allgather_signals(int M, int K, int N);
+
+/*
  * No counterpart in the reference: device buffers shared between the processes of one node with
  * CUDA IPC, the destinations of g16_gemm_scatter. g16_ipc_alloc allocates `bytes` on the current
  * device (cudaMalloc, so the buffer starts an allocation of its own and its handle maps it

@@ -137,16 +137,18 @@ def _exchange_worker(rank, world, port, case, multicast, ret):
 MC, PEER = "_FakeMulticast", "_FakePeer"
 
 
+# Each rank builds two multicast buffers (output slots and completion counter), so a failed set-up
+# closes or releases two per rank.
 @pytest.mark.parametrize("case,multicast,want", [
     ({}, None, {0: (MC, 0, 0), 1: (MC, 0, 0)}),
     # one rank without multicast support: nobody allocates, nobody enters the rendezvous
     ({"unsupported": (1,)}, None, {0: (PEER, 0, 0), 1: (PEER, 0, 0)}),
-    # one rank's allocation fails: the other releases its copy locally, no rendezvous
-    ({"fail": (0,)}, None, {0: (PEER, 0, 0), 1: (PEER, 0, 1)}),
-    # the rendezvous gives one rank no multicast address: both close (collectively)
-    ({"no_mc": (1,)}, None, {0: (PEER, 1, 0), 1: (PEER, 1, 0)}),
+    # one rank's first allocation fails: the other releases both its buffers locally, no rendezvous
+    ({"fail": (0,)}, None, {0: (PEER, 0, 0), 1: (PEER, 0, 2)}),
+    # the rendezvous gives one rank no multicast address: both close both buffers (collectively)
+    ({"no_mc": (1,)}, None, {0: (PEER, 2, 0), 1: (PEER, 2, 0)}),
     ({"fail": (1,)}, False, {0: (PEER, 0, 0), 1: (PEER, 0, 0)}),
-    ({"fail": (0,)}, True, {0: ("raised", 0, 0), 1: ("raised", 0, 1)}),
+    ({"fail": (0,)}, True, {0: ("raised", 0, 0), 1: ("raised", 0, 2)}),
     ({"unsupported": (0,)}, True, {0: ("raised", 0, 0), 1: ("raised", 0, 0)}),
 ])
 def test_exchange_buffer_ranks_agree_gloo_world2(case, multicast, want):

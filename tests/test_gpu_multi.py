@@ -3,7 +3,9 @@
 Fused path (fp16 activations, M > 8, NCCL): every rank's GEMM epilogue writes its output tiles into
 both ranks' full output buffers, once through an NVLink multicast address (torch symmetric memory)
 where the GPUs support it, and with stores into each peer's CUDA IPC mapping otherwise (both paths
-are run). The result equals, bit for bit, the same column shards computed on one GPU with g16_gemm
+are run). On the multicast path the kernel's CTAs signal completion through a multicast counter
+and two output slots alternate (no host collective per call): ten calls in a row are exact and no
+completion wait times out. The result equals, bit for bit, the same column shards computed on one GPU with g16_gemm
 and ksplit = 1 (same kernel, same K order), and the fp64 product within the GEMM tolerance; two
 calls in a row check the ordering of buffer reuse.
 Gather path (fused=False): mm_t per shard and one NCCL all-gather; equals the single-GPU shards.
@@ -41,6 +43,7 @@ def _worker(rank, world, port, ret):
     import torch.distributed as dist
 
     import gtx16_fp16 as g
+    from gtx16_fp16 import _native
     from gtx16_fp16.dist import MulticastBuffer, ShardedMatmul, batch_slice, gather_rows, shard_bounds
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -48,6 +51,7 @@ def _worker(rank, world, port, ret):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     results = {}
+    ShardedMatmul.SIGNAL_WAIT_US = 2_000_000  # a wrong counter target fails fast here
     try:
         for mc in (None, False):  # None: NVLink multicast where supported; False: peer stores
             for M, K, N, out_dtype in ((1024, 2048, 4096, torch.float16), (1000, 1024, 4104, torch.float32)):
@@ -68,7 +72,20 @@ def _worker(rank, world, port, ret):
                 if mc is False:
                     results[f"fused {tag} took the peer path"] = not isinstance(fused._bufs[M], MulticastBuffer)
                 else:
-                    ret[f"multicast {rank}"] = isinstance(fused._bufs[M], MulticastBuffer)
+                    is_mc = isinstance(fused._bufs[M], MulticastBuffer)
+                    ret[f"multicast {rank}"] = is_mc
+                    if is_mc:
+                        # ten calls in a row through the counter-based completion wait, each result
+                        # compared (on the calling stream) before the next call, as documented
+                        ok = True
+                        for _ in range(10):
+                            a_next = torch.randn(M, K, device="cuda", generator=gen).half()
+                            y_next = fused(a_next)
+                            want = torch.cat([_shard_gemm_ksplit1(a_next, w[:, b0:b1].contiguous(), out_dtype)
+                                              for b0, b1 in (shard_bounds(N, world, r) for r in range(world))], 1)
+                            ok = ok and torch.equal(y_next, want)
+                        results[f"fused {tag} multicast signals"] = ok
+                        results[f"fused {tag} no wait timed out"] = _native.device_status(clear=True) == _native.OK
                 fused.close()
         # gather path (mm_t per shard + NCCL all-gather)
         gen = torch.Generator(device="cuda").manual_seed(0)
