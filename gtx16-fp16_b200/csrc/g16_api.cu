@@ -46,10 +46,20 @@ int current_device(int* dev) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Workspace layout of g16_mm_t: [split-K partials | x16 | rscale], each part 256-byte aligned.
+// fp32 activations in g16_mm_t: the row rescale as its own pass (rowscale writes the fp16 copy of x
+// that the GEMM reads). G16_FUSED_RESCALE=1 (a build option) makes g16_mm_t use the form fused into
+// the GEMM's A operand instead, wherever that applies (g16_mm_t_fused_rescale): on B200 the fused
+// form measured slower on every shape tried, so it is not the default.
+#ifndef G16_FUSED_RESCALE
+#define G16_FUSED_RESCALE 0
+#endif
+
+// Workspace layout of g16_mm_t: [split-K partials | x16 | rscale | rscale_inv], each part 256-byte
+// aligned. fp32 x: x16 (the fp16 copy of x) with the rowscale pass, rscale_inv with the fused one.
 struct MmLayout {
-  size_t partials_bytes = 0, x16_off = 0, rscale_off = 0, total = 0;
+  size_t partials_bytes = 0, x16_off = 0, rscale_off = 0, rscale_inv_off = 0, total = 0;
   int ksplit = 1;
+  bool fused_rescale = false;
 };
 
 MmLayout mm_layout(int M, int K, int N, int x_dtype, const DeviceInfo& dev) {
@@ -62,10 +72,17 @@ MmLayout mm_layout(int M, int K, int N, int x_dtype, const DeviceInfo& dev) {
     off += L.partials_bytes;
   }
   if (x_dtype == G16_F32) {
-    L.x16_off = off;
-    off += align_up(static_cast<size_t>(M) * K * 2, 256);
+    L.fused_rescale = G16_FUSED_RESCALE && gemm_auto_uses_pair(M, K, N, dev);
+    if (!L.fused_rescale) {
+      L.x16_off = off;
+      off += align_up(static_cast<size_t>(M) * K * 2, 256);
+    }
     L.rscale_off = off;
     off += align_up(static_cast<size_t>(M) * 4, 256);
+    if (L.fused_rescale) {
+      L.rscale_inv_off = off;
+      off += align_up(static_cast<size_t>(M) * 4, 256);
+    }
   }
   L.total = off;
   return L;
@@ -215,6 +232,14 @@ int mm_t_impl(const void* x, int x_dtype, const void* w_t, const float* bias, vo
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const uint16_t* a16 = static_cast<const uint16_t*>(x);
   const float* rscale = nullptr;
+  if (x_dtype == G16_F32 && L.fused_rescale) {
+    float* rs = reinterpret_cast<float*>(ws + L.rscale_off);
+    float* rsi = reinterpret_cast<float*>(ws + L.rscale_inv_off);
+    st = launch_rowamax(static_cast<const float*>(x), rs, rsi, M, K, G16_ROW_SCALE_THRESHOLD, s);
+    if (st != G16_OK) return st;
+    return launch_gemm_pair_f32a(static_cast<const float*>(x), static_cast<const uint16_t*>(w_t), out, out_dtype,
+                                 bias, rs, rsi, M, K, N, s, *dev, act);
+  }
   if (x_dtype == G16_F32) {
     uint16_t* x16 = reinterpret_cast<uint16_t*>(ws + L.x16_off);
     float* rs = reinterpret_cast<float*>(ws + L.rscale_off);
@@ -241,6 +266,33 @@ int g16_mm_t_act(const void* x, int x_dtype, const void* w_t, const float* bias,
                  int K, int N, int act, void* workspace, size_t workspace_bytes, void* stream) {
   if (act != G16_ACT_NONE && act != G16_ACT_GELU) return G16_ERR_ARG;
   return mm_t_impl(x, x_dtype, w_t, bias, out, out_dtype, M, K, N, workspace, workspace_bytes, stream, act);
+}
+
+size_t g16_mm_t_fused_rescale_workspace_bytes(int M) {
+  return M > 0 ? 2 * align_up(static_cast<size_t>(M) * 4, 256) : 0;
+}
+
+int g16_mm_t_fused_rescale(const float* x, const void* w_t, const float* bias, void* out, int out_dtype, int M,
+                           int K, int N, int act, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_common(x, G16_F32, w_t, out, out_dtype, M, K, N);
+  if (st != G16_OK) return st;
+  if (act != G16_ACT_NONE && act != G16_ACT_GELU) return G16_ERR_ARG;
+  if (M == 0 || N == 0) return G16_OK;
+  if (K == 0) return G16_ERR_UNSUPPORTED;
+  if (bias != nullptr && !aligned16(bias)) return G16_ERR_ALIGN;
+  const DeviceInfo* dev = device_info(&st);
+  if (dev == nullptr) return st;
+  if (M <= G16_SKINNY_MAX_M || !gemm_pair_available()) return G16_ERR_UNSUPPORTED;
+  const size_t need = g16_mm_t_fused_rescale_workspace_bytes(M);
+  if (workspace == nullptr || workspace_bytes < need) return G16_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return G16_ERR_ALIGN;
+  float* rs = static_cast<float*>(workspace);
+  float* rsi = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need / 2);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = launch_rowamax(x, rs, rsi, M, K, G16_ROW_SCALE_THRESHOLD, s);
+  if (st != G16_OK) return st;
+  return launch_gemm_pair_f32a(x, static_cast<const uint16_t*>(w_t), out, out_dtype, bias, rs, rsi, M, K, N, s, *dev,
+                               act);
 }
 
 int g16_skinny(const void* x, int x_dtype, const uint16_t* w_t, const float* bias, void* out, int out_dtype, int M,

@@ -524,6 +524,13 @@ int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev) {
   return ks < 1 ? 1 : ks;
 }
 
+bool gemm_auto_uses_pair(int M, int K, int N, const DeviceInfo& dev) {
+  if (M <= kMidMaxM || K <= 0 || N <= 0) return false;           // medium-M kernel
+  if (plan_gemm_small(M, K, N, dev).bn != 0) return false;        // small-problem kernel
+  if (gemm_auto_ksplit(M, K, N, dev) > 1) return false;           // split K
+  return gemm_pair_available();
+}
+
 size_t gemm_workspace_bytes(int M, int K, int N, int ksplit) {
   if (ksplit <= 1) return 0;
   const int kblocks = (K + kBK - 1) / kBK;

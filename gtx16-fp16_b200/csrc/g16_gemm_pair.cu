@@ -31,20 +31,44 @@ namespace {
 
 constexpr int kPrThreads = 192;
 constexpr int kPrEpiWarps = 4;
-constexpr int kPrStages = 6;
 constexpr uint32_t kPrABytes = kBM * kBK * 2;       // this CTA's 128 rows x 64 k: 16 KiB
 constexpr uint32_t kPrBBoxBytes = kBK * 64 * 2;     // [64 k x 64 n]: 8 KiB
-constexpr uint32_t kPrBBytes = 2 * kPrBBoxBytes;    // this CTA's 128-column half of B
-constexpr uint32_t kPrStageBytes = kPrABytes + kPrBBytes;  // 32 KiB per CTA
-constexpr uint32_t kPrTmemCols = 2 * kBN;           // two 256-column accumulators
 // Rasterisation: 8 pair-rows (2048 rows) per group. Measured against 4 and 16 at 16384^3,
 // 8192 x 8192 x 16384, 4096 x 4096 x 16384 and 16384 x 16384 x 8192: best or within the
 // run-to-run spread on each.
 constexpr int kPrGroupM = 8;
 constexpr uint32_t kPrEpiBufBytes = 32 * 128;             // one warp's 32 rows x 128 bytes
 constexpr uint32_t kPrEpiBytes = kPrEpiWarps * 2 * kPrEpiBufBytes;  // two buffers per epilogue warp
-constexpr size_t kPrSmemBytes = 1024 + kPrStages * kPrStageBytes + kPrEpiBytes + 256;
-static_assert(kPrSmemBytes <= 227 * 1024, "pair GEMM shared memory");
+
+// Tile width BN (the MMA's N): 256 (the default: fewest operand bytes per FLOP) or 128 (twice the
+// tiles, for outputs whose 256 x 256 tiles would leave most SMs idle). Each CTA of the pair holds
+// BN / 2 columns of B per K step; the ring keeps about the same bytes in flight at either width.
+//
+// fp32 activations (A_F32): A is fp32 in global memory and every CTA converts its own rows. TMA
+// loads each K step's [128 x 64] fp32 block (two [128 x 32] boxes, 128-byte swizzle) into a
+// three-deep staging ring; four converter warps (one thread per row) scale it by the row's exact
+// power-of-two reciprocal 1/S (from the row-amax pre-pass), round it to fp16 exactly as the
+// rowscale kernel does, and write the 128-byte-swizzled K-major operand into a two-deep ring of
+// its own, then arrive on the leader's barrier; B has its own TMA ring. The fp16 copy of x never
+// exists in global memory, and the operand bits equal rowscale's, so results equal the two-pass
+// form bit for bit.
+template <int BN, bool A_F32 = false>
+struct PairGeo {
+  static_assert(BN == 128 || BN == 256, "pair tile width");
+  static constexpr int kThreads = A_F32 ? kPrThreads + 128 : kPrThreads;  // + 4 converter warps
+  static constexpr int kBBoxes = BN / 128;                         // [64 k x 64 n] boxes per CTA
+  static constexpr uint32_t kBBytes = kBBoxes * kPrBBoxBytes;      // this CTA's half of B
+  // TMA ring stage: A and B (fp16 A), or B alone (fp32 A: the converted A has a ring of its own)
+  static constexpr uint32_t kStageBytes = A_F32 ? kBBytes : kPrABytes + kBBytes;
+  static constexpr int kStages = A_F32 ? (BN == 256 ? 4 : 8) : (BN == 256 ? 6 : 8);
+  static constexpr int kA16Stages = A_F32 ? 4 : 0;                 // converted fp16 A ring
+  static constexpr int kStgStages = A_F32 ? 2 : 0;                 // fp32 A staging ring
+  static constexpr uint32_t kStgBytes = 2 * kBM * 32 * 4;          // [128 x 64] fp32: 32 KiB
+  static constexpr uint32_t kTmemCols = 2 * BN;                    // two accumulators
+  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kA16Stages * kPrABytes +
+                                       kStgStages * kStgBytes + kPrEpiBytes + 256;
+  static_assert(kSmemBytes <= 227 * 1024, "pair GEMM shared memory");
+};
 
 // Output tensor maps: one for a plain GEMM, or one per destination of the multi-GPU scatter (each
 // [M, col0 + N] of a [.., ldc] buffer; this GEMM's tile lands at column col0 of every one).
@@ -67,9 +91,10 @@ struct PairArgs {
   void* out;
   const float* bias;
   const float* rscale;
+  const float* rscale_inv;  // A_F32 only: 1 / rscale, the factor the converters apply
   int* status;
   int M, N, K;
-  int m2_tiles, n_tiles, units, kblocks;  // tiles of 256 x 256
+  int m2_tiles, n_tiles, units, kblocks;  // tiles of 256 x BN
   int act;                                // epilogue activation (G16_ACT_*)
 };
 
@@ -117,21 +142,32 @@ __device__ __forceinline__ void pair_pack32(const PairArgs& a, int col0, float r
 }
 
 // grid = 2 * pairs CTAs, clusters of 2 along x: CTA 2p + q is rank q of pair p.
-template <bool OUT_F16>
-__global__ void __launch_bounds__(kPrThreads, 1)
+template <bool OUT_F16, int BN, bool A_F32>
+__global__ void __launch_bounds__(PairGeo<BN, A_F32>::kThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const __grid_constant__ PairDst dst,
                  const PairArgs args) {
+  using G = PairGeo<BN, A_F32>;
+  constexpr int kPrStages = G::kStages;
+  constexpr uint32_t kPrStageBytes = G::kStageBytes;
+  constexpr int kStg = G::kStgStages;
+  constexpr int kA16 = G::kA16Stages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* ring = smem;
-  uint8_t* epi_stage = smem + kPrStages * kPrStageBytes;  // 1024-byte aligned
+  uint8_t* ring = smem;                                    // all offsets below 1024-byte aligned
+  uint8_t* a16r = smem + kPrStages * kPrStageBytes;        // converted A ring (A_F32)
+  uint8_t* stg = a16r + kA16 * kPrABytes;                  // fp32 A staging (A_F32)
+  uint8_t* epi_stage = stg + kStg * G::kStgBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_stage + kPrEpiBytes);
   uint64_t* empty_bar = full_bar + kPrStages;
   uint64_t* tfull_bar = empty_bar + kPrStages;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* stg_full = drain_bar + 1;                      // kStg each (A_F32)
+  uint64_t* stg_empty = stg_full + kStg;
+  uint64_t* a16_full = stg_empty + kStg;                   // kA16 each (A_F32)
+  uint64_t* a16_empty = a16_full + kA16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a16_empty + kA16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Uniform over the grid: every CTA returns before any barrier, cluster barrier or allocation.
   if (static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) >
@@ -150,8 +186,16 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPrStages; ++s) {
-      mbar_init(&full_bar[s], 1);   // the leader's producer arrives (expecting both CTAs' bytes)
+      mbar_init(&full_bar[s], 1);   // the leader's producer arrives (expecting both CTAs' TMA bytes)
       mbar_init(&empty_bar[s], 1);  // the leader's MMA commit
+    }
+    for (int j = 0; j < kStg; ++j) {
+      mbar_init(&stg_full[j], 1);   // this CTA's producer (fp32 A bytes)
+      mbar_init(&stg_empty[j], 4);  // this CTA's converter warps
+    }
+    for (int j = 0; j < kA16; ++j) {
+      mbar_init(&a16_full[j], 2 * 4);  // the converter warps of both CTAs (the leader's is used)
+      mbar_init(&a16_empty[j], 1);     // the leader's MMA commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
@@ -167,7 +211,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     for (int d = 0; d < dst.ndst; ++d) tma_prefetch_desc(&dst.m[d]);  // none in multicast mode
   }
   if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, kPrTmemCols);
+    tmem_alloc_pair(tmem_slot, G::kTmemCols);
     tmem_relinquish_pair();
   }
   tc_fence_before();
@@ -181,11 +225,29 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed = 0, armed_phase = 0;
+      int sj = 0;                  // A_F32: staging slot
+      uint32_t sphase = 0;
+      uint32_t sarmed = 0, sarmed_phase = 0;
       bool ok = true;
       for (int u = pair; u < args.units && ok; u += pairs) {
         int mt2, nt;
         pair_coords(args, u, &mt2, &nt);
+        const int row0 = mt2 * 2 * kBM + static_cast<int>(q) * kBM;
         for (int kb = 0; kb < args.kblocks; ++kb) {
+          if constexpr (A_F32) {
+            // this CTA's fp32 rows of the K step, two [128 x 32] boxes, on its own staging barrier
+            if (!mbar_wait(&stg_empty[sj], sphase ^ 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&stg_full[sj], G::kStgBytes);
+            sarmed |= 1u << sj;
+            sarmed_phase = (sarmed_phase & ~(1u << sj)) | (sphase << sj);
+            uint8_t* sdst = stg + sj * G::kStgBytes;
+            tma_load_2d(sdst, &tmap_a, &stg_full[sj], kb * kBK, row0);
+            tma_load_2d(sdst + G::kStgBytes / 2, &tmap_a, &stg_full[sj], kb * kBK + 32, row0);
+            if (++sj == kStg) { sj = 0; sphase ^= 1u; }
+          }
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -197,11 +259,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           }
           const uint32_t bar = map_cluster(smem_u32(&full_bar[stage]), 0);
           uint8_t* sa = ring + stage * kPrStageBytes;
-          uint8_t* sb = sa + kPrABytes;
-          tma_load_2d_pair(sa, &tmap_a, bar, kb * kBK, mt2 * 2 * kBM + static_cast<int>(q) * kBM);
+          uint8_t* sb = A_F32 ? sa : sa + kPrABytes;
+          if constexpr (!A_F32) tma_load_2d_pair(sa, &tmap_a, bar, kb * kBK, row0);
 #pragma unroll
-          for (int j = 0; j < 2; ++j)
-            tma_load_2d_pair(sb + j * kPrBBoxBytes, &tmap_b, bar, nt * kBN + static_cast<int>(q) * (kBN / 2) + 64 * j,
+          for (int j = 0; j < G::kBBoxes; ++j)
+            tma_load_2d_pair(sb + j * kPrBBoxBytes, &tmap_b, bar, nt * BN + static_cast<int>(q) * (BN / 2) + 64 * j,
                              kb * kBK);
           if (++stage == kPrStages) { stage = 0; phase ^= 1u; }
         }
@@ -210,7 +272,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         *abort_flag = 1;
         atomicExch(args.status, G16_ERR_TIMEOUT);
         // The leader's full barriers count both CTAs' bytes: wait for every armed stage, so no
-        // copy is still landing when the pair passes its final cluster barrier.
+        // copy is still landing when the pair passes its final cluster barrier; the same for this
+        // CTA's armed fp32 staging slots.
+        for (int j = 0; j < kStg; ++j)
+          if ((sarmed >> j) & 1u) mbar_wait(&stg_full[j], (sarmed_phase >> j) & 1u, nullptr);
         for (int s = 0; s < kPrStages; ++s)
           if ((armed >> s) & 1u) mbar_wait(&full_bar[s], (armed_phase >> s) & 1u, nullptr);
       }
@@ -218,31 +283,40 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA) ----------------
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = idesc_f16_f32(2 * kBM, kBN, /*b_mn_major=*/true);
+      constexpr uint32_t idesc = idesc_f16_f32(2 * kBM, BN, /*b_mn_major=*/true);
       int stage = 0;
       uint32_t phase = 0;
+      int ai = 0;                  // A_F32: converted-A slot
+      uint32_t aphase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int u = pair; u < args.units && ok; u += pairs) {
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * kBN);
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < args.kblocks; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          bool full = mbar_wait(&full_bar[stage], phase, abort_flag);
+          // A_F32: the converters of both CTAs arrive with release.cluster after writing the operand
+          if constexpr (A_F32) full = full && mbar_wait_acq_cluster(&a16_full[ai], aphase, abort_flag);
+          if (!full) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = smem_u32(ring + stage * kPrStageBytes);
-          const uint32_t sb = sa + kPrABytes;
+          const uint32_t sa = A_F32 ? smem_u32(a16r + ai * kPrABytes) : smem_u32(ring + stage * kPrStageBytes);
+          const uint32_t sb = A_F32 ? smem_u32(ring + stage * kPrStageBytes) : sa + kPrABytes;
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
             // A: K-major, 128-byte rows, 8-row atoms 1024 B apart (SBO); K steps of 32 B.
             const uint64_t adesc = smem_desc_sw128(sa + k * (kUmmaK * 2), 16, 1024);
-            // B: N-major, the two 64-column boxes 8 KiB apart (LBO), 8-row k groups 1024 B (SBO).
+            // B: N-major, 64-column boxes 8 KiB apart (LBO), 8-row k groups 1024 B (SBO).
             const uint64_t bdesc = smem_desc_sw128(sb + k * (kUmmaK * 128), kPrBBoxBytes, 1024);
             umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair(&empty_bar[stage], kPairMask);
           if (++stage == kPrStages) { stage = 0; phase ^= 1u; }
+          if constexpr (A_F32) {
+            umma_commit_pair(&a16_empty[ai], kPairMask);
+            if (++ai == kA16) { ai = 0; aphase ^= 1u; }
+          }
         }
         if (!ok) break;
         umma_commit_pair(&tfull_bar[acc], kPairMask);
@@ -254,7 +328,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       }
       umma_commit_pair(drain_bar, kPairMask);  // every issued MMA complete, in both CTAs
     }
-  } else {
+  } else if (warp < 6) {
     // ---------------- epilogue (warps 2..5, both CTAs) ----------------
     const int quarter = warp & 3;
     const int r_local = quarter * 32 + lane;
@@ -280,11 +354,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       tc_fence_after();
       const int row = mt2 * 2 * kBM + static_cast<int>(q) * kBM + r_local;
       const float rs = (args.rscale != nullptr && row < args.M) ? __ldg(args.rscale + row) : 1.f;
-      const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int y = mt2 * 2 * kBM + static_cast<int>(q) * kBM + quarter * 32;  // the warp's first row
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += kCols, ++nbuf) {
-        const int gcol = nt * kBN + c0;
+      for (int c0 = 0; c0 < BN; c0 += kCols, ++nbuf) {
+        const int gcol = nt * BN + c0;
         uint4 packed[8];
 #pragma unroll
         for (int h = 0; h < kCols / 32; ++h) {
@@ -334,9 +408,72 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     }
   }
 
+  if constexpr (A_F32) {
+    if (warp >= 6) {
+      // ---------------- converters (warps 6..9, both CTAs): fp32 A -> scaled fp16 operand ----------------
+      const int ct = threadIdx.x - 6 * 32;  // this thread's row of the CTA's 128
+      const uint32_t rsw = static_cast<uint32_t>(ct & 7);
+      const uint32_t a16_full_leader0 = map_cluster(smem_u32(&a16_full[0]), 0);
+      int ai = 0, sj = 0;
+      uint32_t aphase = 0, sphase = 0;
+      for (int u = pair; u < args.units; u += pairs) {
+        int mt2, nt;
+        pair_coords(args, u, &mt2, &nt);
+        const int row = mt2 * 2 * kBM + static_cast<int>(q) * kBM + ct;
+        const float inv = row < args.M ? __ldg(args.rscale_inv + row) : 1.f;
+        bool ok = true;
+        for (int kb = 0; kb < args.kblocks; ++kb) {
+          ok = mbar_wait(&stg_full[sj], sphase, abort_flag) && mbar_wait(&a16_empty[ai], aphase ^ 1u, abort_flag);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          // row ct: staged as two [128 x 32] fp32 boxes, chunk c (4 floats) of a row at
+          // ((c ^ (row & 7)) << 4); the operand row holds 8 chunks of 8 fp16 at ((c ^ (row & 7)) << 4)
+          const uint8_t* srow = stg + sj * G::kStgBytes + ct * 128;
+          uint8_t* drow = a16r + ai * kPrABytes + ct * 128;
+#pragma unroll
+          for (int c16 = 0; c16 < 8; ++c16) {
+            const uint8_t* sbox = srow + (c16 >> 2) * (G::kStgBytes / 2);
+            const uint32_t f0 = 2u * static_cast<uint32_t>(c16 & 3);
+            float4 lo = *reinterpret_cast<const float4*>(sbox + ((f0 ^ rsw) << 4));
+            float4 hi = *reinterpret_cast<const float4*>(sbox + (((f0 + 1u) ^ rsw) << 4));
+            if (inv != 1.f) {  // the rowscale kernel's arithmetic: x * (1/S), then round to fp16
+              lo.x *= inv; lo.y *= inv; lo.z *= inv; lo.w *= inv;
+              hi.x *= inv; hi.y *= inv; hi.z *= inv; hi.w *= inv;
+            }
+            const __half2 h0 = __floats2half2_rn(lo.x, lo.y), h1 = __floats2half2_rn(lo.z, lo.w);
+            const __half2 h2 = __floats2half2_rn(hi.x, hi.y), h3 = __floats2half2_rn(hi.z, hi.w);
+            uint4 o;
+            o.x = *reinterpret_cast<const uint32_t*>(&h0);
+            o.y = *reinterpret_cast<const uint32_t*>(&h1);
+            o.z = *reinterpret_cast<const uint32_t*>(&h2);
+            o.w = *reinterpret_cast<const uint32_t*>(&h3);
+            *reinterpret_cast<uint4*>(drow + ((static_cast<uint32_t>(c16) ^ rsw) << 4)) = o;
+          }
+          // the operand (this CTA's shared memory, generic-proxy writes) is read by the tensor core
+          // through the async proxy; the release.cluster arrive below orders it for the leader
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive_cluster(a16_full_leader0 + 8u * static_cast<uint32_t>(ai));
+            mbar_arrive(&stg_empty[sj]);
+          }
+          if (++ai == kA16) { ai = 0; aphase ^= 1u; }
+          if (++sj == kStg) { sj = 0; sphase ^= 1u; }
+        }
+        if (!ok) {
+          if (lane == 0) {
+            *abort_flag = 1;
+            atomicExch(args.status, G16_ERR_TIMEOUT);
+          }
+          break;
+        }
+      }
+    }
+  }
+
   // Every tile store has completed (and, for peer destinations, is visible system-wide) before the
   // grid ends. In multicast mode every lane stored, so every lane fences.
-  if (warp >= 2) {
+  if (warp >= 2 && warp < 6) {
     if (lane == 0) bulk_wait_group0();
     if (dst.ndst == 0 || (dst.ndst > 1 && lane == 0)) __threadfence_system();
   }
@@ -356,23 +493,55 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc_pair(tmem, kPrTmemCols);
+    tmem_dealloc_pair(tmem, G::kTmemCols);
   }
 }
 
 template <typename F>
-cudaError_t ensure_pair_attr(F* kern, std::atomic<uint64_t>& done) {
+cudaError_t ensure_pair_attr(F* kern, std::atomic<uint64_t>& done, size_t bytes) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (dev & 63);
   if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kPrSmemBytes));
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
   if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
   return e;
 }
 
-std::atomic<uint64_t> g_pair_attr16{0}, g_pair_attr32{0};
+// cudaFuncSetAttribute once per (kernel variant, device), then the launch.
+template <bool OUT_F16, int BN, bool A_F32>
+cudaError_t launch_pair_variant(cudaLaunchConfig_t cfg, const CUtensorMap& ta, const CUtensorMap& tb,
+                                const PairDst& dmaps, const PairArgs& args) {
+  using G = PairGeo<BN, A_F32>;
+  static std::atomic<uint64_t> attr_done{0};
+  cudaError_t e = ensure_pair_attr(gemm_pair_kernel<OUT_F16, BN, A_F32>, attr_done, G::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  cfg.blockDim = dim3(G::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = G::kSmemBytes;
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OUT_F16, BN, A_F32>, ta, tb, dmaps, args);
+}
+
+template <bool A_F32>
+cudaError_t launch_pair_any(int out_dtype, int bn, const cudaLaunchConfig_t& cfg, const CUtensorMap& ta,
+                            const CUtensorMap& tb, const PairDst& dmaps, const PairArgs& args) {
+  if (bn == 256)
+    return out_dtype == G16_F16 ? launch_pair_variant<true, 256, A_F32>(cfg, ta, tb, dmaps, args)
+                                : launch_pair_variant<false, 256, A_F32>(cfg, ta, tb, dmaps, args);
+  return out_dtype == G16_F16 ? launch_pair_variant<true, 128, A_F32>(cfg, ta, tb, dmaps, args)
+                              : launch_pair_variant<false, 128, A_F32>(cfg, ta, tb, dmaps, args);
+}
+
+// Tile width of the pair kernel: 256. G16_PAIR_BN=128 (a build option) selects 128-wide tiles,
+// which put twice as many pairs to work on outputs with few 256 x 256 tiles. Measured on B200
+// (CUDA graphs, operands rotated through HBM): a 128-wide K step costs about as much as a 256-wide
+// one, so the narrow tiles lost wherever they applied: 2048 x 3072 x 1024 22.7 us (the small-problem
+// kernel 19.9, 256-wide pairs 23.7), 1024^3 12.2 (9.6, 13.8), 2048 x 4096 x 2048 47.5 (31.2 with
+// 256-wide pairs).
+#ifndef G16_PAIR_BN
+#define G16_PAIR_BN 256
+#endif
+int pair_tile_width(int, int, int) { return G16_PAIR_BN == 128 ? 128 : 256; }
 
 }  // namespace
 
@@ -383,13 +552,14 @@ bool gemm_pair_available() {
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const uint64_t bit = 1ull << (dev & 63);
   if (known.load(std::memory_order_acquire) & bit) return (ok.load(std::memory_order_acquire) & bit) != 0;
-  bool good = ensure_pair_attr(gemm_pair_kernel<true>, g_pair_attr16) == cudaSuccess &&
-              ensure_pair_attr(gemm_pair_kernel<false>, g_pair_attr32) == cudaSuccess;
+  static std::atomic<uint64_t> attr_probe{0};
+  bool good =
+      ensure_pair_attr(gemm_pair_kernel<true, 256, false>, attr_probe, PairGeo<256>::kSmemBytes) == cudaSuccess;
   if (good) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2, 1, 1);
     cfg.blockDim = dim3(kPrThreads, 1, 1);
-    cfg.dynamicSmemBytes = kPrSmemBytes;
+    cfg.dynamicSmemBytes = PairGeo<256>::kSmemBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -398,7 +568,8 @@ bool gemm_pair_available() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int active = 0;
-    good = cudaOccupancyMaxActiveClusters(&active, gemm_pair_kernel<true>, &cfg) == cudaSuccess && active >= 1;
+    good = cudaOccupancyMaxActiveClusters(&active, gemm_pair_kernel<true, 256, false>, &cfg) == cudaSuccess &&
+           active >= 1;
     (void)cudaGetLastError();
   }
   if (good) ok.fetch_or(bit, std::memory_order_acq_rel);
@@ -408,36 +579,42 @@ bool gemm_pair_available() {
 
 namespace {
 
-int launch_pair_impl(const uint16_t* a16, const uint16_t* b16, const PairDst& dmaps, int out_dtype, const float* bias,
-                     const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act) {
+// a: fp16 A (a_f32 false) or fp32 A with the row scales' reciprocals in rscale_inv (a_f32 true).
+int launch_pair_impl(const void* a, bool a_f32, const uint16_t* b16, const PairDst& dmaps, int out_dtype,
+                     const float* bias, const float* rscale, const float* rscale_inv, int M, int K, int N,
+                     cudaStream_t s, const DeviceInfo& dev, int act) {
   if (M <= 0 || N <= 0) return G16_OK;
+  if (a_f32 && (rscale_inv == nullptr || dmaps.ndst != 1)) return G16_ERR_ARG;
   PairArgs args{};
   args.act = act;
   args.bias = bias;
   args.rscale = rscale;
+  args.rscale_inv = rscale_inv;
   args.status = device_status_ptr();
   if (args.status == nullptr) return G16_ERR_CUDA;
   args.M = M;
   args.N = N;
   args.K = K;
+  const int max_pairs = dev.sm_count / 2;
+  const int bn = pair_tile_width(M, N, max_pairs);
   args.m2_tiles = (M + 2 * kBM - 1) / (2 * kBM);
-  args.n_tiles = (N + kBN - 1) / kBN;
+  args.n_tiles = (N + bn - 1) / bn;
   args.units = args.m2_tiles * args.n_tiles;
   args.kblocks = (K + kBK - 1) / kBK;
   if (args.kblocks < 1) return G16_ERR_ARG;
   CUtensorMap ta, tb;
-  int st = make_tmap_2d(&ta, a16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(M),
-                        static_cast<uint64_t>(K), kBM, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  // A: fp16 [128 x 64] boxes, or fp32 [128 x 32] boxes (two per K step); 128-byte swizzle either way.
+  int st = a_f32 ? make_tmap_2d(&ta, a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, static_cast<uint64_t>(M),
+                                static_cast<uint64_t>(K), kBM, 32, CU_TENSOR_MAP_SWIZZLE_128B)
+                 : make_tmap_2d(&ta, a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(M),
+                                static_cast<uint64_t>(K), kBM, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
   st = make_tmap_2d(&tb, b16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                     kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != G16_OK) return st;
-  const int max_pairs = dev.sm_count / 2;
   const int pairs = args.units < max_pairs ? args.units : max_pairs;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(kPrThreads, 1, 1);
-  cfg.dynamicSmemBytes = kPrSmemBytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -446,14 +623,8 @@ int launch_pair_impl(const uint16_t* a16, const uint16_t* b16, const PairDst& dm
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e;
-  if (out_dtype == G16_F16) {
-    e = ensure_pair_attr(gemm_pair_kernel<true>, g_pair_attr16);
-    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<true>, ta, tb, dmaps, args);
-  } else {
-    e = ensure_pair_attr(gemm_pair_kernel<false>, g_pair_attr32);
-    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, dmaps, args);
-  }
+  const cudaError_t e = a_f32 ? launch_pair_any<true>(out_dtype, bn, cfg, ta, tb, dmaps, args)
+                              : launch_pair_any<false>(out_dtype, bn, cfg, ta, tb, dmaps, args);
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();
   return G16_OK;
@@ -473,7 +644,22 @@ int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int ou
   if (st != G16_OK) return st;
   dmaps.ndst = 1;
   dmaps.col0 = 0;
-  return launch_pair_impl(a16, b16, dmaps, out_dtype, bias, rscale, M, K, N, s, dev, act);
+  return launch_pair_impl(a16, false, b16, dmaps, out_dtype, bias, rscale, nullptr, M, K, N, s, dev, act);
+}
+
+int launch_gemm_pair_f32a(const float* x, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                          const float* rscale, const float* rscale_inv, int M, int K, int N, cudaStream_t s,
+                          const DeviceInfo& dev, int act) {
+  if (M <= 0 || N <= 0) return G16_OK;
+  PairDst dmaps{};
+  const bool f16 = out_dtype == G16_F16;
+  int st = make_tmap_2d(&dmaps.m[0], out, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        f16 ? 2 : 4, static_cast<uint64_t>(M), static_cast<uint64_t>(N), 32, f16 ? 64 : 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != G16_OK) return st;
+  dmaps.ndst = 1;
+  dmaps.col0 = 0;
+  return launch_pair_impl(x, true, b16, dmaps, out_dtype, bias, rscale, rscale_inv, M, K, N, s, dev, act);
 }
 
 int launch_gemm_pair_multimem(const uint16_t* a16, const uint16_t* b16, void* mc, int out_dtype, const float* bias,
@@ -487,13 +673,14 @@ int launch_gemm_pair_multimem(const uint16_t* a16, const uint16_t* b16, void* mc
   dmaps.mc = reinterpret_cast<uint64_t>(mc);
   dmaps.ldc = ldc;
   dmaps.mc_flag = reinterpret_cast<uint64_t>(mc_flag);
-  return launch_pair_impl(a16, b16, dmaps, out_dtype, bias, rscale, M, K, N, s, dev, G16_ACT_NONE);
+  return launch_pair_impl(a16, false, b16, dmaps, out_dtype, bias, rscale, nullptr, M, K, N, s, dev, G16_ACT_NONE);
 }
 
 int gemm_pair_ctas(int M, int N, const DeviceInfo& dev) {
   if (M <= 0 || N <= 0) return 0;
-  const int units = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
   const int max_pairs = dev.sm_count / 2;
+  const int bn = pair_tile_width(M, N, max_pairs);
+  const int units = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + bn - 1) / bn);
   return 2 * (units < max_pairs ? units : max_pairs);
 }
 
@@ -517,7 +704,7 @@ int launch_gemm_pair_scatter(const uint16_t* a16, const uint16_t* b16, void* con
   }
   dmaps.ndst = ndst;
   dmaps.col0 = col0;
-  return launch_pair_impl(a16, b16, dmaps, out_dtype, bias, rscale, M, K, N, s, dev, G16_ACT_NONE);
+  return launch_pair_impl(a16, false, b16, dmaps, out_dtype, bias, rscale, nullptr, M, K, N, s, dev, G16_ACT_NONE);
 }
 
 }  // namespace g16

@@ -39,6 +39,9 @@ int skinny_plan_info(int M, int K, int N, int x_dtype, int* info, const DeviceIn
 
 int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M, int K, float thresh,
                     cudaStream_t s);
+// fp32 activations only: the row scales of launch_rowscale (rscale) and their reciprocals, without
+// writing an fp16 copy of x (for a GEMM that converts x itself).
+int launch_rowamax(const float* x, float* rscale, float* rscale_inv, int M, int K, float thresh, cudaStream_t s);
 
 // Tensor-core GEMM. ksplit = 0: automatic plan (the small-problem kernel when the output has too
 // few tiles for the persistent one; ws must still hold gemm_workspace_bytes(M, K, N,
@@ -54,11 +57,19 @@ int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* d
                         const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
                         int flags, cudaStream_t s, const DeviceInfo& dev);
 int gemm_auto_ksplit(int M, int K, int N, const DeviceInfo& dev);
+// Whether launch_gemm's automatic plan (ksplit = 0) is a single pass on the CTA-pair kernel.
+bool gemm_auto_uses_pair(int M, int K, int N, const DeviceInfo& dev);
 
 // GEMM on CTA pairs (g16_gemm_pair.cu): persistent, 256 x 256 tiles, tcgen05.mma.cta_group::2.
 int launch_gemm_pair(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                      const float* rscale, int M, int K, int N, cudaStream_t s, const DeviceInfo& dev, int act = 0);
 bool gemm_pair_available();
+// The same GEMM with fp32 activations: each CTA converts its rows of x to fp16 as x * rscale_inv[row]
+// (rounded like launch_rowscale) in shared memory; the epilogue multiplies by rscale[row]. Both
+// come from launch_rowamax.
+int launch_gemm_pair_f32a(const float* x, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                          const float* rscale, const float* rscale_inv, int M, int K, int N, cudaStream_t s,
+                          const DeviceInfo& dev, int act = 0);
 // The same kernel storing every output tile into ndst buffers [M, ldc] at column col0 (TMA tile
 // stores; peer buffers for the multi-GPU exchange).
 // The same with every tile written once through an NVLink multicast address covering all ranks'

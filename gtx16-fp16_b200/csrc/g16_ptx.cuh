@@ -88,6 +88,26 @@ __device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, 
   }
 }
 
+// Bounded wait with cluster-scope acquire and the abort short-cut: for a barrier that threads of
+// the other CTA of the cluster arrive on (release.cluster) after writing their shared memory.
+__device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // The wait every pipeline in this library uses: the limit is kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
   return mbar_wait_limit(bar, parity, abort_flag, kWaitLimitNs);
@@ -314,6 +334,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // operand reads, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// The same for shared memory that the other CTA of the cluster reads through the async proxy
+// (a CTA pair's tensor core reads both CTAs' operands).
+__device__ __forceinline__ void fence_proxy_async_cluster() {
+  asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
 }
 
 // Epilogue activation (G16_ACT_*), applied to the fp32 value after the bias. GELU is the exact

@@ -219,7 +219,57 @@ cudaError_t launch_rowscale_warp_any(const void* x, uint16_t* y16, float* rscale
   }
 }
 
+// Row scale only, for a GEMM that converts fp32 activations itself: S[row] and its exact reciprocal
+// Sinv[row], the same values rowscale computes; x is read once and nothing else is written (x stays
+// in L2 for the GEMM when it fits). Warp per row, NV 16-byte loads in flight per lane.
+template <int NV>
+__global__ void __launch_bounds__(kThreads) rowamax_f32_kernel(const float* __restrict__ x, float* __restrict__ S,
+                                                               float* __restrict__ Sinv, int M, int K,
+                                                               float thresh) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (kThreads / 32);
+  const int nvec = K / 4;  // K % 8 == 0
+  for (int row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < M; row += warps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * K);
+    float m = 0.f;
+    for (int j0 = 0; j0 < nvec; j0 += 32 * NV) {
+      float4 v[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int j = j0 + lane + 32 * i;
+        v[i] = j < nvec ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) {
+      float inv;
+      S[row] = pow2_row_scale(m, thresh, &inv);
+      Sinv[row] = inv;
+    }
+  }
+}
+
 }  // namespace
+
+int launch_rowamax(const float* x, float* rscale, float* rscale_inv, int M, int K, float thresh, cudaStream_t s) {
+  if (M <= 0) return G16_OK;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const int rows_per_block = kThreads / 32;
+  int blocks = (M + rows_per_block - 1) / rows_per_block;
+  if (blocks > sms * 8) blocks = sms * 8;
+  rowamax_f32_kernel<8><<<blocks, kThreads, 0, s>>>(x, rscale, rscale_inv, M, K, thresh);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  note_launch();
+  return G16_OK;
+}
 
 int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M, int K, float thresh,
                     cudaStream_t s) {

@@ -33,6 +33,8 @@ SIGNATURES = {
     "g16_mm_t": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "g16_mm_t_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g16_mm_t_act": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P, _Z, _P]),
+    "g16_mm_t_fused_rescale": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _Z, _P]),
+    "g16_mm_t_fused_rescale_workspace_bytes": (_Z, [_I]),
     "g16_skinny": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "g16_rowscale": (_I, [_P, _I, _P, _P, _I, _I, _F, _P]),
     "g16_gemm": (_I, [_P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),

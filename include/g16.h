@@ -76,6 +76,22 @@ int g16_mm_t_act(const void* x, int x_dtype, const void* w_t, const float* bias,
 size_t g16_mm_t_workspace_bytes(int M, int K, int N, int x_dtype);
 
 /*
+ * g16_mm_t for fp32 activations with the per-row overflow rescale fused into the GEMM's A operand
+ * (no counterpart in the reference, whose rowscale is always a separate pass, kernels.py:227-250 /
+ * ops.py:86-90). A read-only pass computes each row's scale S (the rowscale rule) and 1/S without
+ * writing an fp16 copy of x; the CTA-pair GEMM then loads fp32 tiles of x with TMA and converter
+ * warps round x * (1/S) to fp16 in shared memory, the operand the tensor core reads; the epilogue
+ * multiplies by S. The operand bits equal rowscale's, so the result equals g16_mm_t's two-pass form
+ * (rowscale, then the same GEMM) bit for bit. Measured on B200 it is slower than that form (the
+ * conversion, not the bytes, bounds it), so g16_mm_t does not use it. M > 8; the workspace holds
+ * g16_mm_t_fused_rescale_workspace_bytes(M) bytes, 256-byte aligned; act as g16_mm_t_act;
+ * G16_ERR_UNSUPPORTED where the CTA-pair kernel cannot run.
+ */
+int g16_mm_t_fused_rescale(const float* x, const void* w_t, const float* bias, void* out, int out_dtype, int M, int K,
+                           int N, int act, void* workspace, size_t workspace_bytes, void* stream);
+size_t g16_mm_t_fused_rescale_workspace_bytes(int M);
+
+/*
  * Skinny path alone, M in [1, 8]: out[M,N] = x[M,K] @ w_t[K,N] + bias (fp32 accumulate).
  * Replaces skinny_f32in / skinny_f16in (src/gtx16_fp16/kernels.py:163-219) plus the zero-fill and
  * fp16 cast around them (ops.py:78-84). K is split across the CTAs of a thread-block cluster and
