@@ -312,6 +312,35 @@ class MmT(Workload):
             f"fp32 F.linear {rows}x{self.K}x{self.N} (reference linear.py fallback)"
 
 
+class FusedRescale(MmT):
+    """fp32-activation GEMM with the row rescale fused into the GEMM's A operand
+    (g16_mm_t_fused_rescale: row-amax pass + CTA-pair GEMM converting fp32 tiles in shared memory),
+    measured beside mm_t's default two-pass form (rowscale, then the GEMM) on the same inputs."""
+
+    def __init__(self, dev, M, K, N, name, rescale):
+        super().__init__(dev, M, K, N, name, torch.float32, torch.float32, 0.02, 0.0, rescale=rescale)
+        self.metric = f"fused-rescale GEMM TFLOPS ({M}x{K}x{N}, fp32 x, g16_mm_t_fused_rescale)"
+        from gtx16_fp16 import _native
+        self._L = _native.lib()
+        n = int(self._L.g16_mm_t_fused_rescale_workspace_bytes(M))
+        self.ws = torch.empty(max(n, 256), dtype=torch.uint8, device=dev)
+        self.O = torch.empty(M, N, device=dev)
+
+    def config(self):
+        return dict(super().config(), path="row-amax pass + CTA-pair GEMM with fp32-A converter warps")
+
+    def step(self, g16):
+        from gtx16_fp16 import _native
+        j = self.i % self.nsets
+        self.i += 1
+        st = self._L.g16_mm_t_fused_rescale(self.X[j].data_ptr(), self.W[j].data_ptr(), self.b.data_ptr(),
+                                            self.O.data_ptr(), _native.G16_F32, self.M, self.K, self.N,
+                                            _native.ACT_NONE, self.ws.data_ptr(), self.ws.numel(),
+                                            _native.stream_handle(self.dev.index or 0))
+        _native.check(st, "g16_mm_t_fused_rescale")
+        return self.O
+
+
 class ShardedGemm(Workload):
     """16384^3 fp16 GEMM with w_t split by columns over the ranks (1/2/4/8 GPUs):
     each rank holds A (replicated) and its column shard of B and computes its output columns; the
@@ -614,6 +643,9 @@ WORKLOADS = {
     "skinny4x3072": lambda dev, w, r: MmT(dev, 4, 1024, 3072, "skinny4x3072", torch.float32, torch.float32, 0.02, 0.01),
     "rescale": lambda dev, w, r: MmT(dev, 2048, 3072, 1024, "rescale", torch.float32, torch.float32, 0.02, 0.0,
                                      rescale=True),
+    "rescale_fused": lambda dev, w, r: FusedRescale(dev, 2048, 3072, 1024, "rescale_fused", True),
+    "linear768": lambda dev, w, r: MmT(dev, 65536, 768, 768, "linear768", torch.float32, torch.float32, 0.02, 0.0),
+    "linear768_fused": lambda dev, w, r: FusedRescale(dev, 65536, 768, 768, "linear768_fused", False),
     "bert": lambda dev, w, r: Bert(dev, w, r),
     "bert_fused": lambda dev, w, r: Bert(dev, w, r, fuse=True),
     "bert16": lambda dev, w, r: Bert(dev, w, r, half=True),
@@ -1042,7 +1074,7 @@ def main():
     ap.add_argument("--workload", default="gemm4096", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--extra", default=("gemm1024,skinny1,skinny4,skinny,skinny1x3072,skinny4x3072,splitk,splitk64,"
-                                        "rescale,decode16,decode16_eager,bert_fused,bert16"),
+                                        "rescale,rescale_fused,linear768,linear768_fused,decode16,decode16_eager,bert_fused,bert16"),
                     help="comma list of other workloads measured briefly into 'sub' (N=1 only); '' to skip")
     ap.add_argument("--blocks", default="gemm16384,bert",
                     help="comma list of collective blocks every rank runs at every N ('collective'); '' to skip")
