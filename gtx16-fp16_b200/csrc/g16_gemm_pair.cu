@@ -26,11 +26,17 @@
 #include "g16_internal.cuh"
 #include "g16_ptx.cuh"
 
+#ifndef G16_PAIR_BN
+#define G16_PAIR_BN 256
+#endif
+#ifndef G16_PAIR_EPIW
+#define G16_PAIR_EPIW 0
+#endif
+
 namespace g16 {
 namespace {
 
 constexpr int kPrThreads = 192;
-constexpr int kPrEpiWarps = 4;
 constexpr uint32_t kPrABytes = kBM * kBK * 2;       // this CTA's 128 rows x 64 k: 16 KiB
 constexpr uint32_t kPrBBoxBytes = kBK * 64 * 2;     // [64 k x 64 n]: 8 KiB
 // Rasterisation: 8 pair-rows (2048 rows) per group. Measured against 4 and 16 at 16384^3,
@@ -38,7 +44,6 @@ constexpr uint32_t kPrBBoxBytes = kBK * 64 * 2;     // [64 k x 64 n]: 8 KiB
 // run-to-run spread on each.
 constexpr int kPrGroupM = 8;
 constexpr uint32_t kPrEpiBufBytes = 32 * 128;             // one warp's 32 rows x 128 bytes
-constexpr uint32_t kPrEpiBytes = kPrEpiWarps * 2 * kPrEpiBufBytes;  // two buffers per epilogue warp
 
 // Tile width BN (the MMA's N): 256 (the default: fewest operand bytes per FLOP) or 128 (twice the
 // tiles, for outputs whose 256 x 256 tiles would leave most SMs idle). Each CTA of the pair holds
@@ -52,21 +57,27 @@ constexpr uint32_t kPrEpiBytes = kPrEpiWarps * 2 * kPrEpiBufBytes;  // two buffe
 // its own, then arrive on the leader's barrier; B has its own TMA ring. The fp16 copy of x never
 // exists in global memory, and the operand bits equal rowscale's, so results equal the two-pass
 // form bit for bit.
-template <int BN, bool A_F32 = false>
+//
+// Epilogue width EPIW: 4 warps (one per TMEM lane quarter) or 8 (two per quarter, each taking half
+// of the tile's columns), for tiles whose few K steps leave too little mainloop time to hide a
+// 4-warp epilogue (short K, fp32 output).
+template <int BN, bool A_F32 = false, int EPIW = 4>
 struct PairGeo {
   static_assert(BN == 128 || BN == 256, "pair tile width");
-  static constexpr int kThreads = A_F32 ? kPrThreads + 128 : kPrThreads;  // + 4 converter warps
+  static_assert(EPIW == 4 || (EPIW == 8 && !A_F32), "epilogue warps");
+  static constexpr int kThreads = 64 + 32 * EPIW + (A_F32 ? 128 : 0);  // + 4 converter warps
+  static constexpr uint32_t kEpiBytes = EPIW * 2 * kPrEpiBufBytes;     // two buffers per epilogue warp
   static constexpr int kBBoxes = BN / 128;                         // [64 k x 64 n] boxes per CTA
   static constexpr uint32_t kBBytes = kBBoxes * kPrBBoxBytes;      // this CTA's half of B
   // TMA ring stage: A and B (fp16 A), or B alone (fp32 A: the converted A has a ring of its own)
   static constexpr uint32_t kStageBytes = A_F32 ? kBBytes : kPrABytes + kBBytes;
-  static constexpr int kStages = A_F32 ? (BN == 256 ? 4 : 8) : (BN == 256 ? 6 : 8);
+  static constexpr int kStages = A_F32 ? (BN == 256 ? 4 : 8) : (BN == 256 ? (EPIW == 8 ? 5 : 6) : 8);
   static constexpr int kA16Stages = A_F32 ? 4 : 0;                 // converted fp16 A ring
   static constexpr int kStgStages = A_F32 ? 2 : 0;                 // fp32 A staging ring
   static constexpr uint32_t kStgBytes = 2 * kBM * 32 * 4;          // [128 x 64] fp32: 32 KiB
   static constexpr uint32_t kTmemCols = 2 * BN;                    // two accumulators
   static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kA16Stages * kPrABytes +
-                                       kStgStages * kStgBytes + kPrEpiBytes + 256;
+                                       kStgStages * kStgBytes + kEpiBytes + 256;
   static_assert(kSmemBytes <= 227 * 1024, "pair GEMM shared memory");
 };
 
@@ -142,12 +153,12 @@ __device__ __forceinline__ void pair_pack32(const PairArgs& a, int col0, float r
 }
 
 // grid = 2 * pairs CTAs, clusters of 2 along x: CTA 2p + q is rank q of pair p.
-template <bool OUT_F16, int BN, bool A_F32>
-__global__ void __launch_bounds__(PairGeo<BN, A_F32>::kThreads, 1)
+template <bool OUT_F16, int BN, bool A_F32, int EPIW>
+__global__ void __launch_bounds__(PairGeo<BN, A_F32, EPIW>::kThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const __grid_constant__ PairDst dst,
                  const PairArgs args) {
-  using G = PairGeo<BN, A_F32>;
+  using G = PairGeo<BN, A_F32, EPIW>;
   constexpr int kPrStages = G::kStages;
   constexpr uint32_t kPrStageBytes = G::kStageBytes;
   constexpr int kStg = G::kStgStages;
@@ -158,7 +169,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   uint8_t* a16r = smem + kPrStages * kPrStageBytes;        // converted A ring (A_F32)
   uint8_t* stg = a16r + kA16 * kPrABytes;                  // fp32 A staging (A_F32)
   uint8_t* epi_stage = stg + kStg * G::kStgBytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_stage + kPrEpiBytes);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_stage + G::kEpiBytes);
   uint64_t* empty_bar = full_bar + kPrStages;
   uint64_t* tfull_bar = empty_bar + kPrStages;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -199,7 +210,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 2 * kPrEpiWarps);  // both CTAs' epilogue warps (the leader's is used)
+      mbar_init(&tempty_bar[b], 2 * EPIW);  // both CTAs' epilogue warps (the leader's is used)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -328,16 +339,19 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       }
       umma_commit_pair(drain_bar, kPairMask);  // every issued MMA complete, in both CTAs
     }
-  } else if (warp < 6) {
-    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+  } else if (warp < 2 + EPIW) {
+    // ---------------- epilogue (warps 2 .. 1 + EPIW, both CTAs) ----------------
     const int quarter = warp & 3;
+    // with 8 warps, the two warps of a lane quarter take one half of the tile's columns each
+    constexpr int kSpan = BN / (EPIW / 4);
+    const int cbeg = ((warp - 2) >> 2) * kSpan;
     const int r_local = quarter * 32 + lane;
     const uint32_t tempty_leader[2] = {map_cluster(smem_u32(&tempty_bar[0]), 0),
                                        map_cluster(smem_u32(&tempty_bar[1]), 0)};
     int acc = 0;
     uint32_t acc_phase = 0;
     uint32_t nbuf = 0;  // staging buffers used so far by this warp (alternating)
-    uint8_t* my_stage = epi_stage + quarter * 2 * kPrEpiBufBytes;
+    uint8_t* my_stage = epi_stage + (warp - 2) * 2 * kPrEpiBufBytes;
     constexpr int kCols = OUT_F16 ? 64 : 32;  // columns per 128-byte row segment
     for (int u = pair; u < args.units; u += pairs) {
       int mt2, nt;
@@ -357,7 +371,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int y = mt2 * 2 * kBM + static_cast<int>(q) * kBM + quarter * 32;  // the warp's first row
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += kCols, ++nbuf) {
+      for (int c0 = cbeg; c0 < cbeg + kSpan; c0 += kCols, ++nbuf) {
         const int gcol = nt * BN + c0;
         uint4 packed[8];
 #pragma unroll
@@ -409,9 +423,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   }
 
   if constexpr (A_F32) {
-    if (warp >= 6) {
+    if (warp >= 2 + EPIW) {
       // ---------------- converters (warps 6..9, both CTAs): fp32 A -> scaled fp16 operand ----------------
-      const int ct = threadIdx.x - 6 * 32;  // this thread's row of the CTA's 128
+      const int ct = threadIdx.x - (2 + EPIW) * 32;  // this thread's row of the CTA's 128
       const uint32_t rsw = static_cast<uint32_t>(ct & 7);
       const uint32_t a16_full_leader0 = map_cluster(smem_u32(&a16_full[0]), 0);
       int ai = 0, sj = 0;
@@ -473,7 +487,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
 
   // Every tile store has completed (and, for peer destinations, is visible system-wide) before the
   // grid ends. In multicast mode every lane stored, so every lane fences.
-  if (warp >= 2 && warp < 6) {
+  if (warp >= 2 && warp < 2 + EPIW) {
     if (lane == 0) bulk_wait_group0();
     if (dst.ndst == 0 || (dst.ndst > 1 && lane == 0)) __threadfence_system();
   }
@@ -510,26 +524,36 @@ cudaError_t ensure_pair_attr(F* kern, std::atomic<uint64_t>& done, size_t bytes)
 }
 
 // cudaFuncSetAttribute once per (kernel variant, device), then the launch.
-template <bool OUT_F16, int BN, bool A_F32>
+template <bool OUT_F16, int BN, bool A_F32, int EPIW>
 cudaError_t launch_pair_variant(cudaLaunchConfig_t cfg, const CUtensorMap& ta, const CUtensorMap& tb,
                                 const PairDst& dmaps, const PairArgs& args) {
-  using G = PairGeo<BN, A_F32>;
+  using G = PairGeo<BN, A_F32, EPIW>;
   static std::atomic<uint64_t> attr_done{0};
-  cudaError_t e = ensure_pair_attr(gemm_pair_kernel<OUT_F16, BN, A_F32>, attr_done, G::kSmemBytes);
+  cudaError_t e = ensure_pair_attr(gemm_pair_kernel<OUT_F16, BN, A_F32, EPIW>, attr_done, G::kSmemBytes);
   if (e != cudaSuccess) return e;
   cfg.blockDim = dim3(G::kThreads, 1, 1);
   cfg.dynamicSmemBytes = G::kSmemBytes;
-  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OUT_F16, BN, A_F32>, ta, tb, dmaps, args);
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OUT_F16, BN, A_F32, EPIW>, ta, tb, dmaps, args);
 }
 
 template <bool A_F32>
-cudaError_t launch_pair_any(int out_dtype, int bn, const cudaLaunchConfig_t& cfg, const CUtensorMap& ta,
+cudaError_t launch_pair_any(int out_dtype, int bn, int epiw, const cudaLaunchConfig_t& cfg, const CUtensorMap& ta,
                             const CUtensorMap& tb, const PairDst& dmaps, const PairArgs& args) {
-  if (bn == 256)
-    return out_dtype == G16_F16 ? launch_pair_variant<true, 256, A_F32>(cfg, ta, tb, dmaps, args)
-                                : launch_pair_variant<false, 256, A_F32>(cfg, ta, tb, dmaps, args);
-  return out_dtype == G16_F16 ? launch_pair_variant<true, 128, A_F32>(cfg, ta, tb, dmaps, args)
-                              : launch_pair_variant<false, 128, A_F32>(cfg, ta, tb, dmaps, args);
+  const bool f16 = out_dtype == G16_F16;
+#if G16_PAIR_BN == 128
+  if (bn == 128)
+    return f16 ? launch_pair_variant<true, 128, A_F32, 4>(cfg, ta, tb, dmaps, args)
+               : launch_pair_variant<false, 128, A_F32, 4>(cfg, ta, tb, dmaps, args);
+#else
+  (void)bn;
+#endif
+  if constexpr (!A_F32) {
+    if (epiw == 8)
+      return f16 ? launch_pair_variant<true, 256, false, 8>(cfg, ta, tb, dmaps, args)
+                 : launch_pair_variant<false, 256, false, 8>(cfg, ta, tb, dmaps, args);
+  }
+  return f16 ? launch_pair_variant<true, 256, A_F32, 4>(cfg, ta, tb, dmaps, args)
+             : launch_pair_variant<false, 256, A_F32, 4>(cfg, ta, tb, dmaps, args);
 }
 
 // Tile width of the pair kernel: 256. G16_PAIR_BN=128 (a build option) selects 128-wide tiles,
@@ -538,10 +562,19 @@ cudaError_t launch_pair_any(int out_dtype, int bn, const cudaLaunchConfig_t& cfg
 // one, so the narrow tiles lost wherever they applied: 2048 x 3072 x 1024 22.7 us (the small-problem
 // kernel 19.9, 256-wide pairs 23.7), 1024^3 12.2 (9.6, 13.8), 2048 x 4096 x 2048 47.5 (31.2 with
 // 256-wide pairs).
-#ifndef G16_PAIR_BN
-#define G16_PAIR_BN 256
-#endif
 int pair_tile_width(int, int, int) { return G16_PAIR_BN == 128 ? 128 : 256; }
+
+// Epilogue warps for an output: 8 when a tile's K loop is short (at most 16 K steps of 64) and
+// the output fp32, the case where a 4-warp epilogue outlasts the next tile's mainloop; else 4.
+// Measured on B200 (CUDA graphs, operands rotated through HBM, fp32 out), 4 -> 8 warps:
+// 65536 x 768 x 768 91.4 -> 85.3 us, 65536 x 768 x 2304 250.7 -> 233.5, 65536 x 768 x 3072
+// 334.9 -> 310.8, 16384 x 1024 x 4096 176.1 -> 124.2; but 65536 x 3072 x 768 236.2 -> 251.2 and
+// fp16-output shapes level or slower (the ring loses a stage to the second set of staging buffers).
+// G16_PAIR_EPIW (a build option, 0 = this rule) forces 4 or 8.
+int pair_epilogue_warps(int K, int out_dtype) {
+  if (G16_PAIR_EPIW == 4 || G16_PAIR_EPIW == 8) return G16_PAIR_EPIW;
+  return (out_dtype == G16_F32 && K <= 16 * kBK) ? 8 : 4;
+}
 
 }  // namespace
 
@@ -554,7 +587,7 @@ bool gemm_pair_available() {
   if (known.load(std::memory_order_acquire) & bit) return (ok.load(std::memory_order_acquire) & bit) != 0;
   static std::atomic<uint64_t> attr_probe{0};
   bool good =
-      ensure_pair_attr(gemm_pair_kernel<true, 256, false>, attr_probe, PairGeo<256>::kSmemBytes) == cudaSuccess;
+      ensure_pair_attr(gemm_pair_kernel<true, 256, false, 4>, attr_probe, PairGeo<256>::kSmemBytes) == cudaSuccess;
   if (good) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2, 1, 1);
@@ -568,7 +601,7 @@ bool gemm_pair_available() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int active = 0;
-    good = cudaOccupancyMaxActiveClusters(&active, gemm_pair_kernel<true, 256, false>, &cfg) == cudaSuccess &&
+    good = cudaOccupancyMaxActiveClusters(&active, gemm_pair_kernel<true, 256, false, 4>, &cfg) == cudaSuccess &&
            active >= 1;
     (void)cudaGetLastError();
   }
@@ -623,8 +656,9 @@ int launch_pair_impl(const void* a, bool a_f32, const uint16_t* b16, const PairD
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = a_f32 ? launch_pair_any<true>(out_dtype, bn, cfg, ta, tb, dmaps, args)
-                              : launch_pair_any<false>(out_dtype, bn, cfg, ta, tb, dmaps, args);
+  const int epiw = a_f32 ? 4 : pair_epilogue_warps(K, out_dtype);
+  const cudaError_t e = a_f32 ? launch_pair_any<true>(out_dtype, bn, epiw, cfg, ta, tb, dmaps, args)
+                              : launch_pair_any<false>(out_dtype, bn, epiw, cfg, ta, tb, dmaps, args);
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();
   return G16_OK;
