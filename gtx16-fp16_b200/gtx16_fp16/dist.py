@@ -327,8 +327,8 @@ class ShardedMatmul:
     def __call__(self, a: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """The full [M, N] output on every rank. On the fused path the returned tensor is one of
         this instance's output buffers for M rows: it stays valid until this rank's next call with
-        the same M (or ``close()``), and must be read on the calling stream; pass ``out`` to keep a
-        copy."""
+        the same M (or ``close()``), and must be read on the calling stream (make every call of an
+        instance on one stream); pass ``out`` to keep a copy."""
         if self.fused_applies(a):
             return self._fused_call(a, out)
         c_local = self.local(a).contiguous()
