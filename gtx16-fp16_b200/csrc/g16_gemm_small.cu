@@ -1,7 +1,7 @@
 // Tensor-core GEMM for problems with fewer output tiles than SMs: out[M,N] = (A @ B) * rscale[row]
 // + bias[col], A [M,K] fp16 K-major, B [K,N] fp16 N-major, fp32 accumulation in TMEM.
 //
-// One CTA per (tile, K chunk), no persistence. Tiles are 128 x BN (BN = 128 or 256: narrower tiles
+// One CTA per (tile, K chunk), no persistence. Tiles are 128 x BN (BN = 64, 128 or 256: narrower tiles
 // put more CTAs to work when M is small). When K is split into C chunks, the C CTAs of a tile form
 // a thread-block cluster and reduce in distributed shared memory instead of through HBM:
 //   * rank r owns rows [r*rpo, (r+1)*rpo) of the tile (rpo = ceil(128 / C));
@@ -25,11 +25,16 @@
 #include "g16_internal.cuh"
 #include "g16_ptx.cuh"
 
+// 64-wide tiles in the automatic plan (a build option for measuring them against 128-wide ones).
+#ifndef G16_SMALL_BN64
+#define G16_SMALL_BN64 1
+#endif
+
 namespace g16 {
 namespace {
 
 constexpr int kSmThreads = 192;
-constexpr int kSmStages = 4;
+constexpr int kSmStagesDefault = 4;
 constexpr uint32_t kSmABytes = kBM * kBK * 2;      // 16 KiB
 constexpr uint32_t kSmBBoxBytes = kBK * 64 * 2;    // one [64 k x 64 n] box: 8 KiB
 constexpr int kSmMaxCluster = 16;
@@ -39,7 +44,10 @@ template <int BN>
 struct SmallGeo {
   static constexpr uint32_t kBBytes = kBK * BN * 2;
   static constexpr uint32_t kStageBytes = kSmABytes + kBBytes;
-  static constexpr uint32_t kRingBytes = kSmStages * kStageBytes;
+  // 64-wide tiles: a deeper ring, which also keeps the CTA at one per SM (two would share its
+  // bandwidth)
+  static constexpr int kStages = BN == 64 ? 6 : kSmStagesDefault;
+  static constexpr uint32_t kRingBytes = kStages * kStageBytes;
   // partials received by an owner: C x rpo rows x BN fp32, at most (128 + C - 1) rows
   static constexpr uint32_t kRecvBytes = (kBM + kSmMaxCluster) * BN * 4;
   static_assert(kRecvBytes <= kRingBytes, "the freed ring must hold an owner's partials");
@@ -81,6 +89,7 @@ __global__ void __launch_bounds__(kSmThreads, 1)
 gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                   const SmallArgs args) {
   using G = SmallGeo<BN>;
+  constexpr int kSmStages = G::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* ring = smem;
@@ -397,7 +406,8 @@ int active_clusters(int c, int tiles) {
 }
 
 int active_clusters_bn(int bn, int c, int tiles) {
-  return bn == 128 ? active_clusters<128>(c, tiles) : active_clusters<256>(c, tiles);
+  return bn == 64 ? active_clusters<64>(c, tiles)
+                  : bn == 128 ? active_clusters<128>(c, tiles) : active_clusters<256>(c, tiles);
 }
 
 }  // namespace
@@ -428,16 +438,36 @@ SmallPlan plan_gemm_small(int M, int K, int N, const DeviceInfo& dev) {
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  const int tiles = m_tiles * ((N + 127) / 128);
-  if (tiles <= dev.sm_count) {
+  // K chunks for `tiles` tiles of width bn: towards one CTA per SM, chunks of >= kmin k-blocks,
+  // every cluster resident at once; 0 if not even one cluster of one CTA fits.
+  auto chunks = [&](int bn, int tiles) {
     const int kmin = tiles < 32 ? 4 : 16;
     int c = std::min(std::min(dev.sm_count / tiles, kSmMaxCluster), std::max(1, kblocks / kmin));
     c = std::max(c, 1);
     for (; c > 1; --c)
-      if (active_clusters_bn(128, c, tiles) >= tiles) break;
-    if (c > 1 || active_clusters_bn(128, 1, tiles) >= 1) {
+      if (active_clusters_bn(bn, c, tiles) >= tiles) break;
+    return (c > 1 || active_clusters_bn(bn, 1, tiles) >= 1) ? c : 0;
+  };
+  const int tiles = m_tiles * ((N + 127) / 128);
+  if (tiles <= dev.sm_count) {
+    const int c = chunks(128, tiles);
+    if (c > 0) {
       p.bn = 128;
       p.csize = c;
+    }
+    // 64-wide tiles when the 128-wide plan leaves more than a quarter of the SMs idle (the cluster
+    // size, at most 16 and further limited by residency, caps the K split) and they put at least
+    // 1.5x as many CTAs to work. Measured on B200 (CUDA graphs, operands rotated through HBM),
+    // 128-wide -> 64-wide: 1024^3 9.56 -> 8.32 us (64 -> 128 CTAs), 200 x 1032 x 136 9.59 -> 6.74
+    // (16 -> 24); but 128 x 16384 x 1024 17.88 -> 18.51 and 256 x 16384 x 512 17.23 -> 18.20, where
+    // residency cuts the 64-wide clusters to 6 chunks (80 -> 96 CTAs).
+    const int tiles64 = m_tiles * ((N + 63) / 64);
+    if (4 * tiles * c < 3 * dev.sm_count && tiles64 <= dev.sm_count && G16_SMALL_BN64) {
+      const int c64 = chunks(64, tiles64);
+      if (c64 > 0 && 2 * tiles64 * c64 >= 3 * tiles * c) {
+        p.bn = 64;
+        p.csize = c64;
+      }
     }
   }
   std::lock_guard<std::mutex> lk(mu);
@@ -448,11 +478,14 @@ SmallPlan plan_gemm_small(int M, int K, int N, const DeviceInfo& dev) {
 int launch_gemm_small(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                       const float* rscale, int M, int K, int N, int bn, int csize, bool exact, cudaStream_t s,
                       int act) {
-  if (csize < 1 || csize > kSmMaxCluster || (bn != 128 && bn != 256)) return G16_ERR_ARG;
+  if (csize < 1 || csize > kSmMaxCluster || (bn != 64 && bn != 128 && bn != 256)) return G16_ERR_ARG;
   const int tiles = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
   int c = csize;
   while (c > 1 && active_clusters_bn(bn, c, tiles) < 1) --c;  // a cluster must fit at all
   if (exact && c != csize) return G16_ERR_UNSUPPORTED;        // the caller asked for csize K chunks
+  if (bn == 64)
+    return out_dtype == G16_F16 ? launch_small_t<true, 64>(a16, b16, out, bias, rscale, M, K, N, c, s, act)
+                                : launch_small_t<false, 64>(a16, b16, out, bias, rscale, M, K, N, c, s, act);
   if (out_dtype == G16_F16) {
     return bn == 128 ? launch_small_t<true, 128>(a16, b16, out, bias, rscale, M, K, N, c, s, act)
                      : launch_small_t<true, 256>(a16, b16, out, bias, rscale, M, K, N, c, s, act);

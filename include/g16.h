@@ -233,7 +233,7 @@ int g16_ipc_close(void* ptr);
  * counterpart in the reference, whose choice is the split-K rule of ops.py:92-101): info[0] = 2 the
  * medium-M kernel (M <= 64: weight columns as the MMA's M, 128-column strips) / 1 the
  * small-problem kernel (one CTA per tile and K chunk) / 0 the persistent kernels, [1] tile width
- * (128 or 256; the strip width for kind 2), [2] K chunks (cluster size; for the persistent kernel
+ * (64, 128 or 256; the strip width for kind 2), [2] K chunks (cluster size; for the persistent kernel
  * the workspace split). info must hold 3 ints. */
 int g16_gemm_plan(int M, int K, int N, int* info);
 
