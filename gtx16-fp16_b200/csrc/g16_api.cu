@@ -67,8 +67,9 @@ MmLayout mm_layout(int M, int K, int N, int x_dtype, const DeviceInfo& dev) {
   if (M <= G16_SKINNY_MAX_M || K == 0) return L;
   L.ksplit = gemm_auto_ksplit(M, K, N, dev);
   size_t off = 0;
-  if (L.ksplit > 1) {
-    L.partials_bytes = align_up(gemm_workspace_bytes(M, K, N, L.ksplit), 256);
+  const size_t partials = gemm_auto_workspace_bytes(M, K, N, dev);
+  if (partials > 0) {
+    L.partials_bytes = align_up(partials, 256);
     off += L.partials_bytes;
   }
   if (x_dtype == G16_F32) {
@@ -191,7 +192,7 @@ size_t g16_gemm_workspace_bytes(int M, int K, int N, int ksplit) {
     int st = G16_OK;
     const DeviceInfo* dev = device_info(&st);
     if (dev == nullptr) return 0;
-    ksplit = gemm_auto_ksplit(M, K, N, *dev);
+    return gemm_auto_workspace_bytes(M, K, N, *dev);
   }
   return gemm_workspace_bytes(M, K, N, ksplit);
 }
@@ -252,7 +253,7 @@ int mm_t_impl(const void* x, int x_dtype, const void* w_t, const float* bias, vo
   // the way the reference's fp16 partial sums could.
   // ksplit 0: the automatic plan (L.ksplit sized the workspace for its fallback).
   return launch_gemm(a16, static_cast<const uint16_t*>(w_t), out, out_dtype, bias, rscale, M, K, N, 0,
-                     L.ksplit > 1 ? ws : nullptr, L.partials_bytes, s, *dev, act);
+                     L.partials_bytes > 0 ? ws : nullptr, L.partials_bytes, s, *dev, act);
 }
 
 }  // namespace
@@ -410,6 +411,12 @@ int g16_gemm_plan(int M, int K, int N, int* info) {
     return G16_OK;
   }
   const SmallPlan p = plan_gemm_small(M, K, N, *dev);
+  if (p.bn != 0 && p.gs_split > 1) {
+    info[0] = 3;
+    info[1] = p.gs_bn;
+    info[2] = p.gs_split;
+    return G16_OK;
+  }
   info[0] = p.bn != 0 ? 1 : 0;
   info[1] = p.bn != 0 ? p.bn : kBN;
   info[2] = p.bn != 0 ? p.csize : gemm_auto_ksplit(M, K, N, *dev);

@@ -538,6 +538,14 @@ size_t gemm_workspace_bytes(int M, int K, int N, int ksplit) {
   return partial_bytes(tiles_of(M, N), ksplit);
 }
 
+size_t gemm_auto_workspace_bytes(int M, int K, int N, const DeviceInfo& dev) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t split = gemm_workspace_bytes(M, K, N, gemm_auto_ksplit(M, K, N, dev));
+  if (M <= kMidMaxM && G16_MIDM_DISPATCH && gemm_midm_ranks(M, K, N, dev) > 0) return split;
+  const size_t gs = small_gs_workspace_bytes(plan_gemm_small(M, K, N, dev), M, N);
+  return gs > split ? gs : split;
+}
+
 namespace {
 
 // cudaFuncSetAttribute once per (kernel, device): the call costs microseconds on the host.
@@ -601,6 +609,12 @@ int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dty
   if (ksplit == 0) {
     const SmallPlan p = plan_gemm_small(M, K, N, dev);
     if (p.bn != 0) {
+      // The grid split when the workspace holds it, else the cluster plan (no workspace).
+      if (p.gs_split > 1 && ws != nullptr && ws_bytes >= small_gs_workspace_bytes(p, M, N) &&
+          (reinterpret_cast<uintptr_t>(ws) & 255u) == 0) {
+        const int st = launch_gemm_small_gs(a16, b16, out, out_dtype, bias, rscale, M, K, N, p, ws, ws_bytes, s, act);
+        if (st != G16_ERR_UNSUPPORTED) return st;
+      }
       const int st = launch_gemm_small(a16, b16, out, out_dtype, bias, rscale, M, K, N, p.bn, p.csize, false, s, act);
       if (st != G16_ERR_UNSUPPORTED) return st;
     }

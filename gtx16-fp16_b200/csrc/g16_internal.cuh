@@ -44,14 +44,17 @@ int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, in
 int launch_rowamax(const float* x, float* rscale, float* rscale_inv, int M, int K, float thresh, cudaStream_t s);
 
 // Tensor-core GEMM. ksplit = 0: automatic plan (the small-problem kernel when the output has too
-// few tiles for the persistent one; ws must still hold gemm_workspace_bytes(M, K, N,
-// gemm_auto_ksplit(...)) for the fallback). ksplit 2..16: that many K chunks reduced in a cluster
-// (same chunks and order as the workspace path, which runs when such a cluster cannot be resident
-// or ksplit > 16; ws must then hold gemm_workspace_bytes(M, K, N, ksplit)).
+// few tiles for the persistent one: its grid split when ws holds gemm_auto_workspace_bytes(), else
+// its cluster plan; ws must hold gemm_workspace_bytes(M, K, N, gemm_auto_ksplit(...)) for the
+// fallback). ksplit 2..16: that many K chunks reduced in a cluster (same chunks and order as the
+// workspace path, which runs when such a cluster cannot be resident or ksplit > 16; ws must then
+// hold gemm_workspace_bytes(M, K, N, ksplit)).
 int launch_gemm(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                 const float* rscale, int M, int K, int N, int ksplit, void* ws, size_t ws_bytes, cudaStream_t s,
                 const DeviceInfo& dev, int act = 0);
 size_t gemm_workspace_bytes(int M, int K, int N, int ksplit);
+// Workspace of the automatic plan (ksplit = 0): its fallback split and the grid split, if any.
+size_t gemm_auto_workspace_bytes(int M, int K, int N, const DeviceInfo& dev);
 // Sharded GEMM whose fp16/fp32 output tiles go to ndst buffers [M, ldc] at column col0 (no split-K).
 int launch_gemm_scatter(const uint16_t* a16, const uint16_t* b16, void* const* dst, int ndst, int out_dtype,
                         const float* bias, const float* rscale, int M, int K, int N, long long ldc, int col0,
@@ -95,10 +98,18 @@ int gemm_midm_ranks(int M, int K, int N, const DeviceInfo& dev);
 // Small-problem GEMM (g16_gemm_small.cu): one CTA per (tile, K chunk), K chunks of a tile reduced
 // inside a thread-block cluster. bn = 0: the problem has enough tiles for the persistent kernel.
 struct SmallPlan {
-  int bn = 0;     // 128 or 256 (N width of a tile)
+  int bn = 0;     // 64, 128 or 256 (N width of a tile)
   int csize = 1;  // K chunks = cluster size
+  // Grid split, used instead when the caller gives a workspace of small_gs_workspace_bytes():
+  // gs_split (>= 2) K chunks of gs_bn-wide tiles as independent CTAs, reduced through the workspace.
+  int gs_bn = 0;
+  int gs_split = 0;
 };
 SmallPlan plan_gemm_small(int M, int K, int N, const DeviceInfo& dev);
+size_t small_gs_workspace_bytes(const SmallPlan& p, int M, int N);  // 0 without a grid split
+int launch_gemm_small_gs(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
+                         const float* rscale, int M, int K, int N, const SmallPlan& p, void* ws, size_t ws_bytes,
+                         cudaStream_t s, int act = 0);
 // exact: fail with G16_ERR_UNSUPPORTED rather than run fewer K chunks than csize.
 int launch_gemm_small(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype, const float* bias,
                       const float* rscale, int M, int K, int N, int bn, int csize, bool exact, cudaStream_t s, int act = 0);

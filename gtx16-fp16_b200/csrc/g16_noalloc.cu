@@ -6,12 +6,13 @@
 // cudaMalloc/cudaFree on latency-critical threads because those calls can synchronise the device.
 // Such callers cannot provide the workspace that g16_gemm needs for its split-K partial tiles.
 //
-// This variant runs g16_gemm's own plan. Most plans need no scratch at all; the one that does, the
-// split into fp32 partial tiles reduced by a second kernel, keeps those tiles in one fixed array in
-// device memory instead of a workspace: g16_static_scratch below, 8 MiB, i.e. at most 64 partial
-// tiles of 128 x 256 fp32. Every GPU that loads this library holds the array until the process
-// exits. An explicit split whose partials do not fit is rejected with G16_ERR_TOO_LARGE; the
-// automatic plan lowers such a split until they fit.
+// This variant runs g16_gemm's own plan. Most plans need no scratch at all; the ones that do (the
+// small-problem grid split, and the split into fp32 partial tiles reduced by a second kernel)
+// keep their partial tiles in one fixed array in device memory instead of a workspace:
+// g16_static_scratch below, 8 MiB, i.e. at most 64 partial tiles of 128 x 256 fp32. Every GPU that
+// loads this library holds the array until the process exits. An explicit split whose partials do
+// not fit is rejected with G16_ERR_TOO_LARGE; in the automatic plan the grid split gives way to the
+// cluster plan when its partials do not fit, and a partial-tile split is lowered until they fit.
 //
 // The array is shared by every call on a device and keeps whatever the last call wrote. Nothing in
 // it has to start at zero: each call writes every partial tile it later reads. Two calls whose
@@ -63,11 +64,12 @@ size_t partials_bytes(int M, int K, int N, int ksplit) { return gemm_workspace_b
 using namespace g16;
 
 // The plan is g16_gemm's own: launch_gemm is called with the static array as its workspace. Most
-// plans need no workspace at all (the medium-M kernel, the small-problem and in-cluster split
-// kernels, single passes); only the partial-tile split (ksplit > 16, or a split whose cluster
-// cannot be resident) uses the array, and launch_gemm checks that its partials fit before it
-// launches anything (G16_ERR_WORKSPACE, nothing enqueued). So the same arguments give the same
-// kernel and the same bits as g16_gemm whenever the partials fit.
+// plans need no workspace at all (the medium-M kernel, the small-problem cluster plan and the
+// in-cluster split, single passes); the grid split runs only where its partials fit the array
+// (else the cluster plan), and the partial-tile split (ksplit > 16, or a split whose cluster cannot
+// be resident) is checked to fit before anything is launched (G16_ERR_WORKSPACE, nothing
+// enqueued). So the same arguments give the same kernel and the same bits as g16_gemm given an
+// 8 MiB workspace.
 extern "C" int g16_gemm_static_scratch(const uint16_t* a16, const uint16_t* b16, void* out, int out_dtype,
                                        const float* bias, const float* rscale, int M, int K, int N, int ksplit,
                                        void* stream) {

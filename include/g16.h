@@ -113,8 +113,11 @@ int g16_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, int M
  * automatically: for M <= 64 a kernel with the operands swapped (128 weight columns per CTA as
  * the MMA's M, the rows as its N, K split over a cluster and reduced in shared memory); else,
  * when the output has too few 128 x 256 tiles to fill the GPU, a kernel with one CTA per (tile,
- * K chunk), 128- or 256-wide tiles and the K chunks of a tile reduced inside a thread-block
- * cluster (no workspace used); otherwise the persistent kernels. ksplit = 1 forces a
+ * K chunk), 64-, 128- or 256-wide tiles and the K chunks of a tile reduced inside a thread-block
+ * cluster (no workspace used) or, for a handful of tiles with a long K and a workspace of
+ * g16_gemm_workspace_bytes(M,K,N,0) given, as independent CTAs reduced through the workspace (the
+ * "grid split"; the workspace needs no initial contents, and calls that may overlap on the GPU
+ * need separate workspaces); otherwise the persistent kernels. ksplit = 1 forces a
  * single pass; ksplit > 1 forces that many K chunks: 2..16 are reduced in a cluster when one can
  * be resident, else (and for ksplit > 16) through the workspace, which must hold
  * g16_gemm_workspace_bytes(M,K,N,ksplit). Both reductions add the chunks' fp32 partials in chunk
@@ -134,13 +137,16 @@ int g16_gemm_auto_ksplit(int M, int K, int N);
  * No counterpart in the reference: an entry point for callers that cannot allocate device memory
  * at call time (e.g. servers that reserve all GPU memory for their own pools at start-up, or hosts
  * that keep cudaMalloc/cudaFree, which can synchronise the device, off latency-critical threads).
- * Same operation, arguments and launch plan as g16_gemm without a workspace: the plans that need
- * none (medium-M, small-problem and in-cluster split kernels, single passes) run as they do there;
- * the partial-tile split (ksplit > 16, or a split whose cluster cannot be resident) keeps its fp32
- * partial tiles in a fixed array in device memory of G16_STATIC_SCRATCH_BYTES (8 MiB, 64 partial
- * tiles of 128 x 256), held by every GPU that loads the library until exit. An explicit split
- * whose partials do not fit returns G16_ERR_TOO_LARGE with nothing launched; with ksplit = 0 such
- * a split is lowered until its partials fit (only then can the bits differ from g16_gemm's).
+ * Same operation, arguments and launch plan as g16_gemm given a workspace of
+ * G16_STATIC_SCRATCH_BYTES: the plans that need none (medium-M, small-problem and in-cluster split
+ * kernels, single passes) run as they do there; the plans that need one (the small-problem grid
+ * split when its partials fit, and the partial-tile split: ksplit > 16, or a split whose cluster
+ * cannot be resident) keep their fp32 partial tiles in a fixed array in device memory of
+ * G16_STATIC_SCRATCH_BYTES (8 MiB, 64 partial tiles of 128 x 256), held by every GPU that loads
+ * the library until exit. An explicit split whose partials do not fit returns G16_ERR_TOO_LARGE
+ * with nothing launched; with ksplit = 0 the grid split gives way to the cluster plan when its
+ * partials do not fit, and a partial-tile split is lowered until they do (so the bits equal those
+ * of g16_gemm with an 8 MiB workspace, and can differ from g16_gemm with a larger one).
  * Allocates nothing. The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.
  * All calls on a device share the array: nothing in it needs to start at zero, but calls that
@@ -231,8 +237,10 @@ int g16_ipc_close(void* ptr);
 
 /* Plan g16_gemm uses for ksplit = 0 on the current device (introspection for tests and tuning; no
  * counterpart in the reference, whose choice is the split-K rule of ops.py:92-101): info[0] = 2 the
- * medium-M kernel (M <= 64: weight columns as the MMA's M, 128-column strips) / 1 the
- * small-problem kernel (one CTA per tile and K chunk) / 0 the persistent kernels, [1] tile width
+ * medium-M kernel (M <= 64: weight columns as the MMA's M, 128-column strips) / 3 the
+ * small-problem kernel's grid split (K chunks as independent CTAs reduced through the workspace;
+ * without a workspace the cluster plan of kind 1 runs instead) / 1 the small-problem kernel (one
+ * CTA per tile and K chunk, chunks reduced in a cluster) / 0 the persistent kernels, [1] tile width
  * (64, 128 or 256; the strip width for kind 2), [2] K chunks (cluster size; for the persistent kernel
  * the workspace split). info must hold 3 ints. */
 int g16_gemm_plan(int M, int K, int N, int* info);

@@ -3,11 +3,12 @@ call time (for example a server that reserved all GPU memory for its own pools a
 g16_gemm's plan, but the one plan that needs scratch memory, the split into fp32 partial tiles,
 keeps them in a fixed 8 MiB array inside libg16 instead of a caller workspace.
 
-Checked through the C ABI against the workspace-based g16_gemm with the same arguments, on two calls
-in a row (the second on new inputs, so whatever the first call left in the shared array must not
-leak into the result). The cases with ksplit > 16 run the partial-tile split, the path that reads
-and writes the array; the others check that the plans needing no scratch are g16_gemm's own. This
-file is collected last on purpose."""
+Checked through the C ABI against the workspace-based g16_gemm with the same arguments (for the
+automatic plan, with a workspace no larger than the array), on two calls in a row (the second on
+new inputs, so whatever the first call left in the shared array must not leak into the result).
+The cases with ksplit > 16 run the partial-tile split and 128 x 3840 x 1024 the grid split, the
+plans that read and write the array; the others check that the plans needing no scratch are
+g16_gemm's own. This file is collected last on purpose."""
 import pytest
 import torch
 
@@ -18,11 +19,18 @@ from _tol import assert_close_fp64, rel_err, GEMM_NORM
 pytestmark = pytest.mark.gpu
 
 
+STATIC_BYTES = 8 << 20  # G16_STATIC_SCRATCH_BYTES
+
+
 def _gemm_with_workspace(a, b, bias, out_dtype, ksplit):
+    """g16_gemm with a workspace of at most the static array's size: the automatic plan then takes
+    the same branches as g16_gemm_static_scratch (the grid split only where its partials fit)."""
     L = _native.lib()
     M, K = a.shape
     N = b.shape[1]
     nws = int(L.g16_gemm_workspace_bytes(M, K, N, ksplit))
+    if ksplit == 0:
+        nws = min(nws, STATIC_BYTES)
     ws = torch.empty(max(nws, 256), dtype=torch.uint8, device=a.device)
     out = torch.empty(M, N, dtype=out_dtype, device=a.device)
     st = L.g16_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), _native.dtype_code(out_dtype),
@@ -58,9 +66,12 @@ def _inputs(M, K, N, seed):
     (200, 8192, 256, 20),    # 2 tiles x 20 chunks = 5 MiB
     (100, 4096, 264, 17),    # 2 tiles, 64 k-blocks: 16 chunks of 4 = 4 MiB, still the partials path
     (64, 16384, 512, 32),    # 2 tiles x 32 = 8 MiB, the whole array
-    # plans without scratch: in-cluster split, automatic plan (medium-M, small-problem)
+    # plans without scratch: in-cluster split, automatic plan (medium-M, small-problem; the grid
+    # split's partials exceed the array at 128 x 16384 x 1024, so the cluster plan runs there)
     (64, 1024, 1024, 4), (128, 16384, 1024, 16), (200, 1032, 136, 3), (1024, 4096, 4096, 2),
     (48, 4096, 768, 0), (2048, 3072, 1024, 0), (128, 16384, 1024, 0),
+    # automatic plan with the grid split inside the array (8 tiles x 15 chunks = 7.5 MiB)
+    (128, 3840, 1024, 0),
 ])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
 def test_static_scratch_matches_workspace_gemm(cuda_ok, M, K, N, ksplit, out_dtype):
