@@ -48,6 +48,12 @@
 #ifndef G16_SMALL_GS
 #define G16_SMALL_GS 1
 #endif
+// Ring depth of the 128-wide tiles. Measured on B200 (CUDA graphs, operands rotated through HBM),
+// 4 -> 5 stages: 128 x 16384 x 1024 13.8 -> 13.3 us, 2048 x 3072 x 1024 19.8 -> 19.3, 128 x 4096 x
+// 4096 15.6 -> 15.0, 512 x 8192 x 1024 19.2 -> 18.8; 6 stages within the run-to-run spread of 5.
+#ifndef G16_SMALL_STAGES128
+#define G16_SMALL_STAGES128 5
+#endif
 
 namespace g16 {
 namespace {
@@ -77,7 +83,7 @@ struct SmallGeo {
   static constexpr uint32_t kStageBytes = kSmABytes + kBBytes;
   // 64-wide tiles: a deeper ring, which also keeps the CTA at one per SM (two would share its
   // bandwidth)
-  static constexpr int kStages = BN == 64 ? 6 : kSmStagesDefault;
+  static constexpr int kStages = BN == 64 ? 6 : BN == 128 ? G16_SMALL_STAGES128 : kSmStagesDefault;
   static constexpr uint32_t kRingBytes = kStages * kStageBytes;
   // partials received by an owner: C x rpo rows x BN fp32, at most (128 + C - 1) rows
   static constexpr uint32_t kRecvBytes = (kBM + kSmMaxCluster) * BN * 4;
