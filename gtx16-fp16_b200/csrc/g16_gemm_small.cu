@@ -18,15 +18,19 @@
 // one cluster of 10 fits in a GPC, so an output of a handful of tiles with a long K
 // (128 x 16384 x 1024: 8 tiles of 128 x 128) keeps most SMs idle under the cluster plan. In GS the
 // S K chunks of a tile are independent CTAs of one wave (at most one CTA per SM, all resident):
-//   * each writes its fp32 partial tile to the workspace, P[tile][chunk][128][BN], staged through
-//     shared memory so every warp store covers whole 128-byte lines;
-//   * then publishes a flag F[tile][chunk] (release) carrying the tile's call tag E[tile] + 1;
-//   * waits (acquire, bounded) until every chunk's flag carries the tag, fetches its share of the
-//     tile (a contiguous 1/S of the partials' quads) from all S partials with bulk copies, adds them
-//     in chunk order (the same order and chunk bounds as the cluster and workspace reductions, so
-//     the same bits), applies the epilogue and stores;
+//   * each writes its fp32 partial tile to the workspace, P[tile][chunk][128][BN], with TMA stores
+//     of [32 x 32] boxes staged in shared memory, waits for them to complete and fences;
+//   * then publishes a flag F[tile][chunk] (its own 128-byte line) carrying the tile's call tag
+//     E[tile] + 1;
+//   * lane s of one warp waits (acquire, bounded) until chunk s's flag carries the tag and then
+//     fetches chunk s's part of this CTA's share (a contiguous 1/S of the tile's quads) with a bulk
+//     copy; the CTA adds the S parts in chunk order (the same order and chunk bounds as the cluster
+//     and workspace reductions, so the same bits), applies the epilogue and stores;
 //   * chunk 0 then advances E[tile], so the next call's tag differs from every flag written so far.
-// Tags make the workspace need no initial contents: stale flags never carry the current tag.
+// Tags make the workspace need no initial contents: stale flags never carry the current tag. The
+// waits rely on all S CTAs of a tile being resident together (the plan checks the occupancy); a
+// grid held back for longer than the wait limit, by another stream's kernels occupying SMs, ends
+// with G16_ERR_TIMEOUT in the status word rather than hanging.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -108,8 +112,12 @@ struct SmallArgs {
 };
 
 template <bool OUT_F16>
-__device__ __forceinline__ void store4_raw(const SmallArgs& a, int row, int col, float o0, float o1, float o2, float o3) {
+__device__ __forceinline__ void store4(const SmallArgs& a, int row, int col, float o0, float o1, float o2, float o3) {
   const size_t off = static_cast<size_t>(row) * a.N + col;
+  o0 = apply_act(o0, a.act);
+  o1 = apply_act(o1, a.act);
+  o2 = apply_act(o2, a.act);
+  o3 = apply_act(o3, a.act);
   if constexpr (OUT_F16) {
     const __half2 h0 = __floats2half2_rn(o0, o1), h1 = __floats2half2_rn(o2, o3);
     uint2 u;
@@ -119,18 +127,6 @@ __device__ __forceinline__ void store4_raw(const SmallArgs& a, int row, int col,
   } else {
     *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + off) = make_float4(o0, o1, o2, o3);
   }
-}
-
-template <bool OUT_F16>
-__device__ __forceinline__ void store4(const SmallArgs& a, int row, int col, float o0, float o1, float o2, float o3) {
-  store4_raw<OUT_F16>(a, row, col, apply_act(o0, a.act), apply_act(o1, a.act), apply_act(o2, a.act),
-                      apply_act(o3, a.act));
-}
-
-// The activation out of line, for a tail that runs once per CTA: its code stays short, so the few
-// instruction-cache lines it needs arrive sooner.
-__device__ __noinline__ float4 act4_outlined(float4 v, int act) {
-  return make_float4(apply_act(v.x, act), apply_act(v.y, act), apply_act(v.z, act), apply_act(v.w, act));
 }
 
 // Grid-split epilogue, run by the four epilogue warps (threads 64..191) once the MMAs have drained.
@@ -261,9 +257,8 @@ __device__ __forceinline__ void gs_epilogue(const SmallArgs& args, const CUtenso
     const float rs = args.rscale != nullptr ? __ldg(args.rscale + orow) : 1.f;
     const float4 b = args.bias != nullptr ? __ldg(reinterpret_cast<const float4*>(args.bias + col))
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 o = make_float4(fmaf(acc.x, rs, b.x), fmaf(acc.y, rs, b.y), fmaf(acc.z, rs, b.z), fmaf(acc.w, rs, b.w));
-    if (args.act != G16_ACT_NONE) o = act4_outlined(o, args.act);
-    store4_raw<OUT_F16>(args, orow, col, o.x, o.y, o.z, o.w);
+    store4<OUT_F16>(args, orow, col, fmaf(acc.x, rs, b.x), fmaf(acc.y, rs, b.y), fmaf(acc.z, rs, b.z),
+                    fmaf(acc.w, rs, b.w));
   }
 }
 
