@@ -376,8 +376,9 @@ def test_rowscale_row_lengths(cuda_ok, xdt, K):
     assert torch.equal(y, (x.float() / S[:, None]).half())
 
 
-# shapes reaching each epilogue: skinny (M <= 8, fp32 x), medium-M, small-problem (cluster split),
-# CTA pairs (N = 12288 included), and the empty reduction
+# shapes reaching each epilogue: skinny (M <= 8, fp32 x), medium-M, small-problem (one chunk at
+# 256 x 768 x 3072; the grid split at 128 x 16384 x 1024, where mm_t gives a workspace), CTA pairs
+# (N = 12288 included), and the empty reduction
 GELU_SHAPES = [(1, 1024, 3072), (4, 4096, 512), (16, 1024, 3072), (64, 768, 3072), (256, 768, 3072),
                (128, 16384, 1024), (4096, 768, 3072), (512, 256, 12288), (40, 0, 136)]
 
