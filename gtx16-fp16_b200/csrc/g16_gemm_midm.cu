@@ -33,6 +33,14 @@
 #include "g16_internal.cuh"
 #include "g16_ptx.cuh"
 
+// K steps (of 64 rows) each rank of the medium-M cluster keeps at least. Measured on B200 (CUDA
+// graphs, weights rotated through HBM), 4 -> 2 -> 1: 64 x 1024 x 1024 7.6 -> 6.8 -> 6.8 us (2 -> 8
+// -> 16 ranks), 16 x 1024 x 1024 5.0 -> 4.7 -> 4.7, 64 x 768 x 768 9.1 -> 7.1 -> 6.3; shapes with
+// long K unchanged (their ranks are capped by the CTAs that fit).
+#ifndef G16_MIDM_MIN_STEPS
+#define G16_MIDM_MIN_STEPS 1
+#endif
+
 namespace g16 {
 namespace {
 
@@ -377,9 +385,9 @@ MidPlan md_plan_shape(int M, int K, int N, int ctas) {
   p.mx = M <= 16 ? 16 : M <= 32 ? 32 : 64;
   p.strips = (N + kMdStrip - 1) / kMdStrip;
   // K ranks: a power of two (the 128 strip columns split evenly among owners), at most 16, with
-  // at least 4 K steps (256 rows) each, and strips x ranks within the CTAs that fit at once.
+  // at least G16_MIDM_MIN_STEPS K steps each, and strips x ranks within the CTAs that fit at once.
   int c = 1;
-  while (2 * c <= kMdMaxCluster && 2 * c * p.strips <= ctas && K >= 2 * c * 4 * kBK) c *= 2;
+  while (2 * c <= kMdMaxCluster && 2 * c * p.strips <= ctas && K >= 2 * c * G16_MIDM_MIN_STEPS * kBK) c *= 2;
   int kchunk = (K + c - 1) / c;
   kchunk = (kchunk + kBK - 1) / kBK * kBK;
   p.csize = c;
