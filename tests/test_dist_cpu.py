@@ -70,7 +70,7 @@ def _worker(rank, world, port, n_total, ret):
 @pytest.mark.parametrize("n_total", [64, 72])  # equal shards / unequal shards
 def test_sharded_matmul_gloo_world2(n_total):
     world = 2
-    ret = mp.Manager().dict()
+    ret = mp.get_context("spawn").Manager().dict()
     mp.spawn(_worker, args=(world, _free_port(), n_total, ret), nprocs=world, join=True)
     assert dict(ret) == {0: True, 1: True}
 
@@ -156,7 +156,7 @@ def test_exchange_buffer_ranks_agree_gloo_world2(case, multicast, want):
     allocation, no multicast address) sends every rank to peer stores with the same collectives;
     multicast=False never tries, multicast=True raises on every rank."""
     world = 2
-    ret = mp.Manager().dict()
+    ret = mp.get_context("spawn").Manager().dict()
     mp.spawn(_exchange_worker, args=(world, _free_port(), case, multicast, ret), nprocs=world, join=True)
     assert dict(ret) == want
 
@@ -190,7 +190,7 @@ def _leaving_worker(rank, world, port, ret):
 
 def test_rank_leaving_between_steps_is_detected_gloo_world2():
     world = 2
-    ret = mp.Manager().dict()
+    ret = mp.get_context("spawn").Manager().dict()
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_leaving_worker, args=(r, world, port, ret)) for r in range(world)]

@@ -110,7 +110,7 @@ def test_sharded_matmul_two_gpus():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
-    ret = mp.Manager().dict()
+    ret = mp.get_context("spawn").Manager().dict()
     mp.spawn(_worker, args=(2, _free_port(), ret), nprocs=2, join=True)
     got = {k: v for k, v in dict(ret).items() if isinstance(k, int)}
     print("multicast path used:", {k: v for k, v in dict(ret).items() if not isinstance(k, int)})
