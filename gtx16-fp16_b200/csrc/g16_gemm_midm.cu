@@ -35,8 +35,9 @@
 
 // K steps (of 64 rows) each rank of the medium-M cluster keeps at least. Measured on B200 (CUDA
 // graphs, weights rotated through HBM), 4 -> 2 -> 1: 64 x 1024 x 1024 7.6 -> 6.8 -> 6.8 us (2 -> 8
-// -> 16 ranks), 16 x 1024 x 1024 5.0 -> 4.7 -> 4.7, 64 x 768 x 768 9.1 -> 7.1 -> 6.3; shapes with
-// long K unchanged (their ranks are capped by the CTAs that fit).
+// ranks; 16 requested at 1, lowered to 8 by the residency check), 16 x 1024 x 1024 5.0 -> 4.7 ->
+// 4.7, 64 x 768 x 768 9.1 -> 7.1 -> 6.3; shapes with long K unchanged (their ranks are capped by
+// the CTAs that fit).
 #ifndef G16_MIDM_MIN_STEPS
 #define G16_MIDM_MIN_STEPS 1
 #endif
