@@ -131,6 +131,10 @@ __global__ void __launch_bounds__(kThreads) rowscale_warp_kernel(const TX* __res
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (kThreads / 32);
   const int nvec = K / kVec;  // K % 8 == 0
+  // Programmatic dependent launch: the next kernel (the GEMM reading y) may start its set-up now;
+  // x, y and S are touched only once the preceding kernel has completed.
+  if (threadIdx.x == 0) grid_launch_dependents();
+  grid_dependency_wait();
   for (int row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < M; row += warps) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * K);
     uint4 v[NV];
@@ -200,9 +204,17 @@ cudaError_t launch_rowscale_warp(const void* x, uint16_t* y16, float* rscale, in
   int blocks = (M + rows_per_block - 1) / rows_per_block;
   const int cap = sms * 8;  // 64 warps per SM, each with NV loads in flight
   if (blocks > cap) blocks = cap;
-  rowscale_warp_kernel<TX, NV><<<blocks, kThreads, 0, s>>>(static_cast<const TX*>(x), reinterpret_cast<__half*>(y16),
-                                                            rscale, M, K, thresh);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, rowscale_warp_kernel<TX, NV>, static_cast<const TX*>(x),
+                            reinterpret_cast<__half*>(y16), rscale, M, K, thresh);
 }
 
 template <typename TX>
