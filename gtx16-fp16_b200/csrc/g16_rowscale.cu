@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(kThreads) rowscale_f32_kernel(const float* __r
   const size_t row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * K);
   const int nv = K / 4;
+  if (threadIdx.x == 0) grid_launch_dependents();  // as in rowscale_warp_kernel
+  grid_dependency_wait();
   float m = 0.f;
   for (int i = threadIdx.x; i < nv; i += kThreads) {
     const float4 v = xr[i];
@@ -94,6 +96,8 @@ __global__ void __launch_bounds__(kThreads) rowscale_f16_kernel(const __half* __
   const size_t row = blockIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
   const int nv = K / 8;
+  if (threadIdx.x == 0) grid_launch_dependents();  // as in rowscale_warp_kernel
+  grid_dependency_wait();
   float m = 0.f;
   for (int i = threadIdx.x; i < nv; i += kThreads) {
     const uint4 v = xr[i];
@@ -294,14 +298,21 @@ int launch_rowscale(const void* x, int x_dtype, uint16_t* y16, float* rscale, in
     note_launch();
     return G16_OK;
   }
-  if (x_dtype == G16_F32) {
-    rowscale_f32_kernel<<<M, kThreads, 0, s>>>(static_cast<const float*>(x), reinterpret_cast<__half*>(y16), rscale,
-                                                K, thresh);
-  } else {
-    rowscale_f16_kernel<<<M, kThreads, 0, s>>>(static_cast<const __half*>(x), reinterpret_cast<__half*>(y16),
-                                                rscale, K, thresh);
-  }
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(M), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      x_dtype == G16_F32
+          ? cudaLaunchKernelEx(&cfg, rowscale_f32_kernel, static_cast<const float*>(x), reinterpret_cast<__half*>(y16),
+                               rscale, K, thresh)
+          : cudaLaunchKernelEx(&cfg, rowscale_f16_kernel, static_cast<const __half*>(x),
+                               reinterpret_cast<__half*>(y16), rscale, K, thresh);
   if (e != cudaSuccess) return cuda_fail(e);
   note_launch();
   return G16_OK;
