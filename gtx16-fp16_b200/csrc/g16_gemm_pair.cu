@@ -43,6 +43,10 @@ constexpr uint32_t kPrBBoxBytes = kBK * 64 * 2;     // [64 k x 64 n]: 8 KiB
 // 8192 x 8192 x 16384, 4096 x 4096 x 16384 and 16384 x 16384 x 8192: best or within the
 // run-to-run spread on each.
 constexpr int kPrGroupM = 8;
+// Programmatic dependent launch of plain-output calls (a build option while it is measured).
+#ifndef G16_PAIR_PDL
+#define G16_PAIR_PDL 1
+#endif
 constexpr uint32_t kPrEpiBufBytes = 32 * 128;             // one warp's 32 rows x 128 bytes
 
 // Tile width BN (the MMA's N): 256 (the default: fewest operand bytes per FLOP) or 128 (twice the
@@ -183,9 +187,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   // Uniform over the grid: every CTA returns before any barrier, cluster barrier or allocation.
   if (static_cast<uint32_t>(reinterpret_cast<const volatile uint8_t*>(abort_flag + 1) - smem_raw) >
       dynamic_smem_bytes()) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(args.status, G16_ERR_ARG);
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+      grid_dependency_wait();
+      atomicExch(args.status, G16_ERR_ARG);
+    }
     return;
   }
+  // The next kernel may start its set-up now; it reads nothing this one writes before its own wait.
+  if (threadIdx.x == 0) grid_launch_dependents();
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -229,6 +238,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   cluster_sync();  // barrier initialisation and the pair's TMEM allocation, visible to both CTAs
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch (plain outputs): the set-up above may overlap the preceding
+  // kernel's tail; no global memory is touched before it has completed.
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
@@ -649,13 +661,16 @@ int launch_pair_impl(const void* a, bool a_f32, const uint16_t* b16, const PairD
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch for a plain output (the multi-GPU variants keep stream order).
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = dmaps.ndst == 1 && G16_PAIR_PDL ? 2 : 1;
   const int epiw = a_f32 ? 4 : pair_epilogue_warps(K, out_dtype);
   const cudaError_t e = a_f32 ? launch_pair_any<true>(out_dtype, bn, epiw, cfg, ta, tb, dmaps, args)
                               : launch_pair_any<false>(out_dtype, bn, epiw, cfg, ta, tb, dmaps, args);
